@@ -1,0 +1,189 @@
+/*
+ * pkv_b200.h -- C ABI of libpagedkv_b200.so, the B200 (sm_100a) device data
+ * path of a paged KV cache.
+ *
+ * This is the drop-in seam for the `KvBackend` trait of paged-kv-core
+ * (crates/paged-kv-core/src/backend.rs:23-124): a host-language backend
+ * implements the trait by calling these functions, beside the unchanged
+ * `CpuBackend`, `BlockAllocator`, `BlockTable` and `Scheduler`. Plain
+ * pointers, sizes and status codes only; no C++ exceptions cross it.
+ *
+ * Pool layout (identical to CpuBackend, crates/paged-kv-core/src/cpu.rs:13-21):
+ * two planes, K and V, each [num_layers][num_blocks][block_size][entry] in
+ * the pool dtype, entry = num_kv_heads*head_dim (or, for shard r of G, the
+ * contiguous slice [r*E/G, (r+1)*E/G) of it).
+ *
+ * Error model: every function returns a pkv_status. The variant's two fields
+ * (e.g. InvalidLayer{layer, num_layers}) and a readable message are kept per
+ * thread; fetch them with pkv_last_error_fields() / pkv_last_error().
+ * Host-buffer entry points validate in the same order as CpuBackend and the
+ * trait's default batch methods, and, like them, leave the effects of the
+ * items before a failing item in place.
+ *
+ * Threading: one backend handle is used by one host thread at a time (the
+ * trait's mutating methods take &mut self). Work is issued on the handle's
+ * own CUDA stream unless a device entry point is given another one.
+ */
+#ifndef PKV_B200_H
+#define PKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* One status per CacheError variant (crates/paged-kv-core/src/error.rs:12-46). */
+typedef enum pkv_status {
+    PKV_OK = 0,
+    PKV_ERR_OUT_OF_BLOCKS = 1,       /* OutOfBlocks{requested, available}  error.rs:14 */
+    PKV_ERR_INVALID_BLOCK = 2,       /* InvalidBlock{id, num_blocks}       error.rs:17 */
+    PKV_ERR_BLOCK_NOT_ALLOCATED = 3, /* BlockNotAllocated{id}              error.rs:20 */
+    PKV_ERR_REFCOUNT_OVERFLOW = 4,   /* RefCountOverflow{id, max}          error.rs:24 */
+    PKV_ERR_SLOT_OUT_OF_RANGE = 5,   /* SlotOutOfRange{slot, block_size}   error.rs:27 */
+    PKV_ERR_SHAPE_MISMATCH = 6,      /* ShapeMismatch{expected, actual}    error.rs:31 */
+    PKV_ERR_INVALID_LAYER = 7,       /* InvalidLayer{layer, num_layers}    error.rs:34 */
+    PKV_ERR_UNKNOWN_SEQUENCE = 8,    /* UnknownSequence{id}                error.rs:38 */
+    PKV_ERR_DEVICE = 9               /* Device(String)                     error.rs:45 */
+} pkv_status;
+
+/* Element types of the pool and of caller buffers. CacheConfig only carries
+ * dtype_bytes (config.rs:19-20); the type tag tells bf16 from f16. */
+typedef enum pkv_dtype { PKV_F32 = 0, PKV_BF16 = 1, PKV_F16 = 2 } pkv_dtype;
+
+/* CacheConfig (crates/paged-kv-core/src/config.rs:8-21), field for field. */
+typedef struct pkv_config {
+    uint64_t num_blocks;
+    uint64_t block_size;
+    uint64_t num_kv_heads;
+    uint64_t head_dim;
+    uint64_t num_layers;
+    uint64_t dtype_bytes;
+} pkv_config;
+
+/* PhysicalSlot (crates/paged-kv-core/src/types.rs:40-43); BlockId widened to 64 bits. */
+typedef struct pkv_slot {
+    uint64_t block;
+    uint64_t slot;
+} pkv_slot;
+
+typedef struct pkv_backend pkv_backend;
+
+/* ---- errors ------------------------------------------------------------ */
+
+/* Message of the last failing call on this thread ("" after success). */
+const char *pkv_last_error(void);
+/* Status of the last call on this thread; writes the variant's two fields
+ * (0 where the variant has fewer). */
+int pkv_last_error_fields(int64_t *field0, int64_t *field1);
+
+/* ---- lifecycle (CudaBackend::new, crates/paged-kv-cuda/src/backend.rs:63-92) ---- */
+
+/* Allocate a zero-filled pool on `device`. dtype must agree with
+ * cfg->dtype_bytes. num_shards = 1 gives the whole pool; otherwise this
+ * backend holds shard `shard_rank` (contiguous entry slice) and every
+ * host/device K/V buffer passed to it holds that slice only. */
+int pkv_create(const pkv_config *cfg, int dtype, int device, int shard_rank, int num_shards,
+               pkv_backend **out);
+int pkv_destroy(pkv_backend *b);
+
+/* ---- metadata ------------------------------------------------------------ */
+
+/* KvBackend::config (backend.rs:25): the full, unsharded geometry. */
+int pkv_get_config(const pkv_backend *b, pkv_config *out);
+/* KvBackend::allocated_bytes (backend.rs:118-120): this backend's pool bytes. */
+uint64_t pkv_allocated_bytes(const pkv_backend *b);
+/* KvBackend::device_name (backend.rs:123); starts with "cuda:". */
+int pkv_device_name(const pkv_backend *b, char *buf, uint64_t buf_len);
+/* Shard geometry: elements per entry held here and their offset in the full entry. */
+int pkv_shard_info(const pkv_backend *b, int *shard_rank, int *num_shards, uint64_t *elem_offset,
+                   uint64_t *shard_entry_elems);
+/* Device addresses of the K and V planes (for attention kernels and checks). */
+int pkv_device_planes(const pkv_backend *b, void **k_plane, void **v_plane);
+
+/* ---- KvBackend methods over host buffers ----------------------------------
+ * Lengths are element counts of the caller's buffers; host_dtype is their
+ * element type. Data converted to a narrower pool type is rounded to nearest
+ * even; widening is exact. The call returns once the host buffers have been
+ * consumed; device work may still be running on the backend's stream. */
+
+/* KvBackend::write_kv (backend.rs:34-40; CpuBackend cpu.rs:95-111). */
+int pkv_write_kv(pkv_backend *b, uint64_t layer, pkv_slot dst, const void *k, uint64_t k_len,
+                 const void *v, uint64_t v_len, int host_dtype);
+/* KvBackend::write_kv_batch (backend.rs:55-74) -> one reshape_and_cache launch
+ * (replaces CudaBackend::write_kv_batch, crates/paged-kv-cuda/src/backend.rs:147-209). */
+int pkv_write_kv_batch(pkv_backend *b, uint64_t layer, const pkv_slot *dsts, uint64_t count,
+                       const void *k, uint64_t k_len, const void *v, uint64_t v_len,
+                       int host_dtype);
+/* KvBackend::read_kv (backend.rs:82-88; cpu.rs:113-129). Synchronous; copies
+ * only the requested entry (the reference copies the whole plane,
+ * crates/paged-kv-cuda/src/backend.rs:211-242). */
+int pkv_read_kv(pkv_backend *b, uint64_t layer, pkv_slot src, void *k_out, uint64_t k_len,
+                void *v_out, uint64_t v_len, int host_dtype);
+/* KvBackend::copy_block (backend.rs:97; cpu.rs:131-149). */
+int pkv_copy_block(pkv_backend *b, uint64_t src, uint64_t dst);
+/* KvBackend::copy_blocks (backend.rs:104-109) -> batched copy_blocks kernel
+ * (replaces crates/paged-kv-cuda/src/backend.rs:251-293). pairs = [count][2]
+ * (src, dst). Same result as applying the pairs one after another, chains
+ * included. */
+int pkv_copy_blocks(pkv_backend *b, const uint64_t *pairs, uint64_t count);
+/* KvBackend::zero_block (backend.rs:115; cpu.rs:151-160;
+ * crates/paged-kv-cuda/src/backend.rs:295-320). */
+int pkv_zero_block(pkv_backend *b, uint64_t block);
+/* Batched zero_block: one launch for many blocks (the reference launches once per block). */
+int pkv_zero_blocks(pkv_backend *b, const uint64_t *blocks, uint64_t count);
+
+/* ---- device entry points (inputs already in device memory) ----------------
+ * stream: a cudaStream_t, or NULL for the backend's own stream. These do not
+ * synchronise. Bad indices found on the device are skipped and recorded in
+ * the backend's device error word (pkv_device_error). */
+
+/* reshape_and_cache (crates/paged-kv-cuda/kernels/kernels.cu:31-60).
+ * layer >= 0: k, v are [num_tokens][entry] rows (row pitch src_token_stride
+ * elements) written into that layer. layer == -1: k, v are
+ * [num_layers][num_tokens][entry] (layer pitch src_layer_stride elements) and
+ * every layer is written in one launch. slot_mapping[t] = block*block_size +
+ * slot; a negative slot skips the token (padding). src_dtype may differ from
+ * the pool dtype (rounded to nearest even when narrowing). */
+int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, const void *v,
+                              int64_t src_token_stride, int64_t src_layer_stride,
+                              const int64_t *slot_mapping, int64_t num_tokens, int src_dtype,
+                              void *stream);
+/* copy_blocks (kernels.cu:62-92). pairs = [count][2] int64 (src, dst) in
+ * device memory. The pairs must not chain (no dst is another pair's src or
+ * dst), which copy-on-write pairs never do; src == dst is a no-op. */
+int pkv_copy_blocks_dev(pkv_backend *b, const int64_t *pairs, int64_t count, void *stream);
+/* zero_block (kernels.cu:94-110), batched: blocks = [count] int64 in device memory. */
+int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, void *stream);
+/* Slot resolution (no device counterpart in the reference; host rule
+ * BlockTable::slot_for_position, block_table.rs:97-101, flattened as
+ * crates/paged-kv-cuda/src/backend.rs:172-175). Sequence q has ctx_lens[q]
+ * cached tokens and new_lens[q] new ones; block_tables is [num_seqs][table_stride]
+ * int32. Writes cu_seqlens[0..num_seqs] (exclusive prefix of new_lens, int32)
+ * and slot_mapping[0..num_tokens). num_tokens must equal sum(new_lens).
+ * Tokens whose logical block lies past table_stride or whose table entry is
+ * outside the pool get slot -1 and are recorded in the device error word. */
+int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t table_stride,
+                          const int32_t *ctx_lens, const int32_t *new_lens, int64_t num_seqs,
+                          int64_t num_tokens, int32_t *cu_seqlens, int64_t *slot_mapping,
+                          void *stream);
+/* Order-independent 64-bit digests of this backend's K and V planes (the
+ * element's global index in the full plane and its f32-widened bits, summed;
+ * zeros contribute nothing). Digests of the shards of one pool add up
+ * (mod 2^64) to the digest of the whole pool. Synchronous. */
+int pkv_digest(pkv_backend *b, uint64_t *k_digest, uint64_t *v_digest, void *stream);
+
+/* Wait for all work issued on the backend's stream. */
+int pkv_sync(pkv_backend *b);
+/* Synchronise, then read and clear the device error word. Returns PKV_OK if no
+ * device entry point met a bad index since the last call; otherwise the
+ * status of the first one met and, in *index, the token/pair/block index it
+ * was met at. */
+int pkv_device_error(pkv_backend *b, int64_t *index);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKV_B200_H */

@@ -1,0 +1,672 @@
+// pkv_backend.cpp -- host side of the B200 KvBackend: validation in the
+// reference's order, staging, copy-pair scheduling and kernel launches.
+
+#include "pkv_backend.hpp"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <limits>
+#include <unordered_map>
+
+namespace pkv {
+
+Status error(int code, int64_t a, int64_t b, std::string msg) {
+    Status s;
+    s.code = code;
+    s.a = a;
+    s.b = b;
+    s.msg = std::move(msg);
+    return s;
+}
+
+Status device_error(const std::string &what, cudaError_t e) {
+    return error(PKV_ERR_DEVICE, 0, 0, what + ": " + cudaGetErrorString(e));
+}
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    int want;
+    explicit DeviceGuard(int d) : want(d) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != want) cudaSetDevice(want);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0 && prev != want) cudaSetDevice(prev);
+    }
+};
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Messages worded as the reference's CacheError Display impl (error.rs:42-76).
+std::string msg_invalid_block(uint64_t id, uint64_t n) {
+    return "invalid block #" + std::to_string(id) + ": pool holds " + std::to_string(n) + " blocks";
+}
+std::string msg_slot(uint64_t slot, uint64_t bs) {
+    return "slot " + std::to_string(slot) + " out of range for block size " + std::to_string(bs);
+}
+std::string msg_shape(uint64_t e, uint64_t a) {
+    return "shape mismatch: expected " + std::to_string(e) + " elements, got " + std::to_string(a);
+}
+std::string msg_layer(uint64_t l, uint64_t n) {
+    return "invalid layer " + std::to_string(l) + ": model has " + std::to_string(n) + " layers";
+}
+
+float host_to_f32(const void *p, uint64_t i, DType t) {
+    switch (t) {
+        case DType::F32: return static_cast<const float *>(p)[i];
+        case DType::BF16: {
+            uint32_t bits = uint32_t(static_cast<const uint16_t *>(p)[i]) << 16;
+            float f;
+            std::memcpy(&f, &bits, 4);
+            return f;
+        }
+        case DType::F16: return __half2float(static_cast<const __half *>(p)[i]);
+    }
+    return 0.f;
+}
+
+void host_from_f32(void *p, uint64_t i, DType t, float f) {
+    switch (t) {
+        case DType::F32: static_cast<float *>(p)[i] = f; break;
+        case DType::BF16: static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(f); break;
+        case DType::F16: static_cast<__half *>(p)[i] = __float2half_rn(f); break;
+    }
+}
+
+// Convert `n` elements between host types (exact when widening, round to
+// nearest even when narrowing); same type is a plain copy.
+void host_convert(void *dst, DType dt, const void *src, DType st, uint64_t n) {
+    if (dt == st) {
+        std::memcpy(dst, src, n * dtype_size(st));
+        return;
+    }
+    for (uint64_t i = 0; i < n; ++i) host_from_f32(dst, i, dt, host_to_f32(src, i, st));
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// construction: CudaBackend::new (crates/paged-kv-cuda/src/backend.rs:63-92)
+
+Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int shard_rank,
+                           int num_shards, std::unique_ptr<B200Backend> *out) {
+    if (static_cast<int>(dtype) < 0 || static_cast<int>(dtype) > 2)
+        return error(PKV_ERR_DEVICE, 0, 0, "invalid config: unknown dtype tag");
+    if (cfg.dtype_bytes != static_cast<uint64_t>(dtype_size(dtype)))
+        return error(PKV_ERR_DEVICE, 0, 0,
+                     "invalid config: dtype_bytes " + std::to_string(cfg.dtype_bytes) +
+                         " does not match the pool dtype (" + std::to_string(dtype_size(dtype)) +
+                         " bytes)");
+    if (num_shards < 1 || shard_rank < 0 || shard_rank >= num_shards)
+        return error(PKV_ERR_DEVICE, 0, 0, "invalid shard: rank " + std::to_string(shard_rank) +
+                                               " of " + std::to_string(num_shards));
+    const uint64_t full_entry = cfg.num_kv_heads * cfg.head_dim;
+    if (full_entry % static_cast<uint64_t>(num_shards) != 0)
+        return error(PKV_ERR_DEVICE, 0, 0,
+                     "invalid shard: entry of " + std::to_string(full_entry) +
+                         " elements does not split into " + std::to_string(num_shards) + " shards");
+    if (cfg.block_size == 0)
+        return error(PKV_ERR_DEVICE, 0, 0, "invalid config: block_size must be positive");
+    // Plane size must fit comfortably in signed 64-bit byte offsets.
+    const long double plane_bytes = (long double)cfg.num_layers * cfg.num_blocks * cfg.block_size *
+                                    (full_entry / num_shards) * dtype_size(dtype);
+    if (plane_bytes > (long double)(1ull << 60))
+        return error(PKV_ERR_DEVICE, 0, 0, "invalid config: pool too large");
+
+    std::unique_ptr<B200Backend> b(new B200Backend());
+    b->cfg_ = cfg;
+    b->dtype_ = dtype;
+    b->device_ = device;
+    b->shard_rank_ = shard_rank;
+    b->num_shards_ = num_shards;
+    b->shard_entry_ = full_entry / num_shards;
+
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return device_error("no CUDA device", e);
+    if (device < 0 || device >= ndev)
+        return error(PKV_ERR_DEVICE, 0, 0, "device " + std::to_string(device) + " not present");
+    DeviceGuard g(device);
+    cudaDeviceProp prop{};
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess)
+        return device_error("cudaGetDeviceProperties", e);
+    b->gpu_name_ = prop.name;
+    b->sms_ = num_sms(device);
+    if ((e = cudaStreamCreateWithFlags(&b->stream_, cudaStreamNonBlocking)) != cudaSuccess)
+        return device_error("cudaStreamCreate", e);
+    if ((e = cudaEventCreateWithFlags(&b->h_stage_free_, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&b->inputs_consumed_, cudaEventDisableTiming)) != cudaSuccess)
+        return device_error("cudaEventCreate", e);
+
+    const size_t plane = static_cast<size_t>(plane_bytes);
+    if (plane > 0) {
+        if ((e = cudaMalloc(&b->k_plane_, plane)) != cudaSuccess ||
+            (e = cudaMalloc(&b->v_plane_, plane)) != cudaSuccess)
+            return device_error("allocating a pool of 2 x " + std::to_string(plane) + " bytes", e);
+        // alloc_zeros (crates/paged-kv-cuda/src/backend.rs:84-85).
+        if ((e = cudaMemsetAsync(b->k_plane_, 0, plane, b->stream_)) != cudaSuccess ||
+            (e = cudaMemsetAsync(b->v_plane_, 0, plane, b->stream_)) != cudaSuccess)
+            return device_error("zeroing the pool", e);
+    }
+    if ((e = cudaMalloc(&b->d_err_, sizeof(DevError) + 2 * sizeof(unsigned long long))) !=
+        cudaSuccess)
+        return device_error("cudaMalloc", e);
+    b->d_digest_ = reinterpret_cast<unsigned long long *>(b->d_err_ + 1);
+    if ((e = cudaMemsetAsync(b->d_err_, 0, sizeof(DevError), b->stream_)) != cudaSuccess)
+        return device_error("cudaMemset", e);
+    if ((e = cudaStreamSynchronize(b->stream_)) != cudaSuccess) return device_error("init", e);
+    *out = std::move(b);
+    return Status::Ok();
+}
+
+B200Backend::~B200Backend() {
+    DeviceGuard g(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (k_plane_) cudaFree(k_plane_);
+    if (v_plane_) cudaFree(v_plane_);
+    if (d_err_) cudaFree(d_err_);
+    if (d_stage_) cudaFree(d_stage_);
+    if (h_stage_) cudaFreeHost(h_stage_);
+    if (h_stage_free_) cudaEventDestroy(h_stage_free_);
+    if (inputs_consumed_) cudaEventDestroy(inputs_consumed_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+Status B200Backend::check(const char *what, cudaError_t e) const {
+    if (e == cudaSuccess) return Status::Ok();
+    return ::pkv::device_error(what, e);
+}
+
+uint64_t B200Backend::allocated_bytes() const {
+    // CacheConfig::total_bytes (config.rs:74-76) for this backend's share of the entry.
+    return 2 * cfg_.num_layers * cfg_.num_blocks * cfg_.block_size * shard_entry_ * cfg_.dtype_bytes;
+}
+
+std::string B200Backend::device_name() const {
+    static const char *names[] = {"f32", "bf16", "f16"};
+    std::string s = "cuda:" + std::to_string(device_) + " (" + gpu_name_ + ", " +
+                    names[static_cast<int>(dtype_)];
+    if (num_shards_ > 1)
+        s += ", shard " + std::to_string(shard_rank_) + "/" + std::to_string(num_shards_);
+    s += ", " + std::to_string(allocated_bytes() / (1024 * 1024)) + " MiB pool)";
+    return s;
+}
+
+// validate_block (cpu.rs:72-80) and validate (cpu.rs:55-70).
+Status B200Backend::validate_block(uint64_t block) const {
+    if (block >= cfg_.num_blocks)
+        return error(PKV_ERR_INVALID_BLOCK, (int64_t)block, (int64_t)cfg_.num_blocks,
+                     msg_invalid_block(block, cfg_.num_blocks));
+    return Status::Ok();
+}
+
+Status B200Backend::validate(uint64_t layer, pkv_slot at) const {
+    if (layer >= cfg_.num_layers)
+        return error(PKV_ERR_INVALID_LAYER, (int64_t)layer, (int64_t)cfg_.num_layers,
+                     msg_layer(layer, cfg_.num_layers));
+    Status s = validate_block(at.block);
+    if (!s.ok()) return s;
+    if (at.slot >= cfg_.block_size)
+        return error(PKV_ERR_SLOT_OUT_OF_RANGE, (int64_t)at.slot, (int64_t)cfg_.block_size,
+                     msg_slot(at.slot, cfg_.block_size));
+    return Status::Ok();
+}
+
+Status B200Backend::ensure_device_stage(size_t bytes) {
+    if (bytes <= d_stage_bytes_) return Status::Ok();
+    cudaError_t e = cudaStreamSynchronize(stream_);  // old buffer may still be read
+    if (e != cudaSuccess) return device_error("cudaStreamSynchronize", e);
+    if (d_stage_) cudaFree(d_stage_);
+    d_stage_ = nullptr;
+    d_stage_bytes_ = 0;
+    const size_t want = std::max(bytes, d_stage_bytes_ + d_stage_bytes_ / 2);
+    if ((e = cudaMalloc(&d_stage_, want)) != cudaSuccess)
+        return device_error("allocating " + std::to_string(want) + " bytes of staging", e);
+    d_stage_bytes_ = want;
+    return Status::Ok();
+}
+
+Status B200Backend::ensure_host_stage(size_t bytes) {
+    cudaError_t e = cudaEventSynchronize(h_stage_free_);
+    if (e != cudaSuccess) return device_error("cudaEventSynchronize", e);
+    if (bytes <= h_stage_bytes_) return Status::Ok();
+    if (h_stage_) cudaFreeHost(h_stage_);
+    h_stage_ = nullptr;
+    h_stage_bytes_ = 0;
+    const size_t want = std::max<size_t>(bytes, 64 * 1024);
+    if ((e = cudaMallocHost(&h_stage_, want)) != cudaSuccess)
+        return device_error("allocating pinned staging", e);
+    h_stage_bytes_ = want;
+    return Status::Ok();
+}
+
+// ---------------------------------------------------------------------------
+// reshape_and_cache over host buffers
+
+Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_t count,
+                                   const void *k, const void *v, DType host) {
+    if (count == 0) return Status::Ok();
+    DeviceGuard g(device_);
+    const size_t row_bytes = shard_entry_ * dtype_size(host);
+    const size_t slot_bytes = round_up(count * sizeof(int64_t), kAlign);
+    const size_t kv_bytes = round_up(count * row_bytes, kAlign);
+    Status s = ensure_device_stage(slot_bytes + 2 * kv_bytes);
+    if (!s.ok()) return s;
+    if (!(s = ensure_host_stage(count * sizeof(int64_t))).ok()) return s;
+
+    // Combined slot index block*block_size + slot (crates/paged-kv-cuda/src/backend.rs:172-175).
+    // Within one batch the last write to a slot wins, as in the sequential
+    // default write_kv_batch; earlier duplicates become padding (-1).
+    int64_t *hs = static_cast<int64_t *>(h_stage_);
+    for (uint64_t i = 0; i < count; ++i) hs[i] = (int64_t)(dsts[i].block * cfg_.block_size + dsts[i].slot);
+    if (count > 1) {
+        if (seen_.size() * 64 < slots_per_layer()) seen_.assign((slots_per_layer() + 63) / 64, 0);
+        for (uint64_t i = count; i-- > 0;) {
+            const uint64_t x = (uint64_t)hs[i];
+            uint64_t &w = seen_[x >> 6];
+            const uint64_t bit = 1ull << (x & 63);
+            if (w & bit) hs[i] = -1;
+            else w |= bit;
+        }
+        for (uint64_t i = 0; i < count; ++i)
+            if (hs[i] >= 0) seen_[(uint64_t)hs[i] >> 6] = 0;
+    }
+    char *d = static_cast<char *>(d_stage_);
+    int64_t *d_slots = reinterpret_cast<int64_t *>(d);
+    char *d_k = d + slot_bytes;
+    char *d_v = d_k + kv_bytes;
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(d_slots, hs, count * sizeof(int64_t), cudaMemcpyHostToDevice, stream_)) ||
+        (e = cudaEventRecord(h_stage_free_, stream_)) ||
+        (e = cudaMemcpyAsync(d_k, k, count * row_bytes, cudaMemcpyHostToDevice, stream_)) ||
+        (e = cudaMemcpyAsync(d_v, v, count * row_bytes, cudaMemcpyHostToDevice, stream_)) ||
+        (e = cudaEventRecord(inputs_consumed_, stream_)))
+        return device_error("staging K/V", e);
+
+    ReshapeLaunch a{};
+    a.k = d_k;
+    a.v = d_v;
+    a.src_token_stride = (long long)shard_entry_;
+    a.src_layer_stride = 0;
+    a.k_pool = k_plane_;
+    a.v_pool = v_plane_;
+    a.first_layer = (long long)layer;
+    a.num_layers = 1;
+    a.slots_per_layer = (long long)slots_per_layer();
+    a.entry_elems = (long long)shard_entry_;
+    a.slots = reinterpret_cast<const long long *>(d_slots);
+    a.num_tokens = (long long)count;
+    a.src_dtype = host;
+    a.pool_dtype = dtype_;
+    a.err = d_err_;
+    if ((e = launch_reshape(a, sms_, stream_)) != cudaSuccess) return device_error("reshape_and_cache", e);
+    // The caller's slices are borrowed: return only once they have been read.
+    if ((e = cudaEventSynchronize(inputs_consumed_)) != cudaSuccess)
+        return device_error("staging K/V", e);
+    return Status::Ok();
+}
+
+// write_kv (cpu.rs:95-111): validate, then K length, then V length.
+Status B200Backend::write_kv(uint64_t layer, pkv_slot dst, const void *k, uint64_t k_len,
+                             const void *v, uint64_t v_len, DType host) {
+    Status s = validate(layer, dst);
+    if (!s.ok()) return s;
+    if (k_len != shard_entry_)
+        return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)shard_entry_, (int64_t)k_len, msg_shape(shard_entry_, k_len));
+    if (v_len != shard_entry_)
+        return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)shard_entry_, (int64_t)v_len, msg_shape(shard_entry_, v_len));
+    return launch_scatter(layer, &dst, 1, k, v, host);
+}
+
+// write_kv_batch (backend.rs:55-74): K shape, V shape, then per-token
+// validation in order; tokens before the first invalid one are written.
+Status B200Backend::write_kv_batch(uint64_t layer, const pkv_slot *dsts, uint64_t count,
+                                   const void *k, uint64_t k_len, const void *v, uint64_t v_len,
+                                   DType host) {
+    const uint64_t expected = count * shard_entry_;
+    if (k_len != expected)
+        return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)expected, (int64_t)k_len, msg_shape(expected, k_len));
+    if (v_len != expected)
+        return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)expected, (int64_t)v_len, msg_shape(expected, v_len));
+    uint64_t valid = 0;
+    Status bad;
+    for (; valid < count; ++valid) {
+        bad = validate(layer, dsts[valid]);
+        if (!bad.ok()) break;
+    }
+    Status s = launch_scatter(layer, dsts, valid, k, v, host);
+    if (!s.ok()) return s;
+    return bad;
+}
+
+// read_kv (cpu.rs:113-129): only the requested entry crosses PCIe.
+Status B200Backend::read_kv(uint64_t layer, pkv_slot src, void *k_out, uint64_t k_len, void *v_out,
+                            uint64_t v_len, DType host) {
+    Status s = validate(layer, src);
+    if (!s.ok()) return s;
+    if (k_len != shard_entry_)
+        return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)shard_entry_, (int64_t)k_len, msg_shape(shard_entry_, k_len));
+    if (v_len != shard_entry_)
+        return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)shard_entry_, (int64_t)v_len, msg_shape(shard_entry_, v_len));
+    DeviceGuard g(device_);
+    const size_t eb = entry_bytes();
+    if (!(s = ensure_host_stage(2 * eb)).ok()) return s;
+    const size_t off = ((layer * cfg_.num_blocks + src.block) * cfg_.block_size + src.slot) * eb;
+    char *h = static_cast<char *>(h_stage_);
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(h, static_cast<char *>(k_plane_) + off, eb, cudaMemcpyDeviceToHost, stream_)) ||
+        (e = cudaMemcpyAsync(h + eb, static_cast<char *>(v_plane_) + off, eb, cudaMemcpyDeviceToHost, stream_)) ||
+        (e = cudaEventRecord(h_stage_free_, stream_)) || (e = cudaStreamSynchronize(stream_)))
+        return device_error("read_kv", e);
+    host_convert(k_out, host, h, dtype_, shard_entry_);
+    host_convert(v_out, host, h + eb, dtype_, shard_entry_);
+    return Status::Ok();
+}
+
+// ---------------------------------------------------------------------------
+// copy_blocks
+
+// Launch pairs (all valid) so that the result equals applying them one after
+// another (backend.rs:104-109). Self-copies are dropped (cpu.rs:134-136).
+// Pairs go into waves: a pair waits for every earlier pair that writes its
+// source, reads its destination or writes its destination. Copy-on-write
+// pairs always have fresh destinations, so they form a single wave.
+Status B200Backend::launch_copy_pairs(const uint64_t *pairs, uint64_t count) {
+    std::vector<int64_t> flat;
+    std::vector<int> wave;
+    flat.reserve(2 * count);
+    wave.reserve(count);
+    std::unordered_map<uint64_t, int> last_write, last_read;
+    int max_wave = 0;
+    for (uint64_t i = 0; i < count; ++i) {
+        const uint64_t src = pairs[2 * i], dst = pairs[2 * i + 1];
+        if (src == dst) continue;
+        int w = 0;
+        auto it = last_write.find(src);
+        if (it != last_write.end()) w = std::max(w, it->second + 1);
+        it = last_read.find(dst);
+        if (it != last_read.end()) w = std::max(w, it->second + 1);
+        it = last_write.find(dst);
+        if (it != last_write.end()) w = std::max(w, it->second + 1);
+        last_write[dst] = w;
+        auto r = last_read.find(src);
+        if (r == last_read.end()) last_read[src] = w;
+        else r->second = std::max(r->second, w);
+        flat.push_back((int64_t)src);
+        flat.push_back((int64_t)dst);
+        wave.push_back(w);
+        max_wave = std::max(max_wave, w);
+    }
+    const uint64_t n = wave.size();
+    if (n == 0) return Status::Ok();
+    DeviceGuard g(device_);
+    Status s = ensure_device_stage(round_up(n * 16, kAlign));
+    if (!s.ok()) return s;
+    if (!(s = ensure_host_stage(n * 16)).ok()) return s;
+    int64_t *h = static_cast<int64_t *>(h_stage_);
+    std::vector<std::pair<uint64_t, uint64_t>> ranges;  // [begin, end) per wave
+    uint64_t pos = 0;
+    for (int w = 0; w <= max_wave; ++w) {
+        const uint64_t begin = pos;
+        for (uint64_t i = 0; i < n; ++i)
+            if (wave[i] == w) {
+                h[2 * pos] = flat[2 * i];
+                h[2 * pos + 1] = flat[2 * i + 1];
+                ++pos;
+            }
+        if (pos > begin) ranges.emplace_back(begin, pos);
+    }
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(d_stage_, h, n * 16, cudaMemcpyHostToDevice, stream_)) ||
+        (e = cudaEventRecord(h_stage_free_, stream_)))
+        return device_error("staging copy pairs", e);
+    for (auto &r : ranges) {
+        CopyLaunch a{};
+        a.k_pool = k_plane_;
+        a.v_pool = v_plane_;
+        a.num_layers = (long long)cfg_.num_layers;
+        a.num_blocks = (long long)cfg_.num_blocks;
+        a.block_bytes = (long long)block_bytes();
+        a.pairs = static_cast<const long long *>(d_stage_) + 2 * r.first;
+        a.num_pairs = (long long)(r.second - r.first);
+        a.err = d_err_;
+        if ((e = launch_copy_blocks(a, stream_)) != cudaSuccess) return device_error("copy_blocks", e);
+    }
+    return Status::Ok();
+}
+
+// copy_block (cpu.rs:131-149).
+Status B200Backend::copy_block(uint64_t src, uint64_t dst) {
+    Status s = validate_block(src);
+    if (!s.ok()) return s;
+    if (!(s = validate_block(dst)).ok()) return s;
+    if (src == dst) return Status::Ok();
+    const uint64_t pair[2] = {src, dst};
+    return launch_copy_pairs(pair, 1);
+}
+
+// copy_blocks (backend.rs:104-109): pairs before the first invalid one apply.
+Status B200Backend::copy_blocks(const uint64_t *pairs, uint64_t count) {
+    uint64_t valid = 0;
+    Status bad;
+    for (; valid < count; ++valid) {
+        bad = validate_block(pairs[2 * valid]);
+        if (!bad.ok()) break;
+        bad = validate_block(pairs[2 * valid + 1]);
+        if (!bad.ok()) break;
+    }
+    Status s = launch_copy_pairs(pairs, valid);
+    if (!s.ok()) return s;
+    return bad;
+}
+
+// ---------------------------------------------------------------------------
+// zero_block
+
+Status B200Backend::launch_zero_ids(const uint64_t *blocks, uint64_t count) {
+    if (count == 0) return Status::Ok();
+    DeviceGuard g(device_);
+    Status s = ensure_device_stage(round_up(count * 8, kAlign));
+    if (!s.ok()) return s;
+    if (!(s = ensure_host_stage(count * 8)).ok()) return s;
+    std::memcpy(h_stage_, blocks, count * 8);
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(d_stage_, h_stage_, count * 8, cudaMemcpyHostToDevice, stream_)) ||
+        (e = cudaEventRecord(h_stage_free_, stream_)))
+        return device_error("staging block ids", e);
+    ZeroLaunch a{};
+    a.k_pool = k_plane_;
+    a.v_pool = v_plane_;
+    a.num_layers = (long long)cfg_.num_layers;
+    a.num_blocks = (long long)cfg_.num_blocks;
+    a.block_bytes = (long long)block_bytes();
+    a.blocks = static_cast<const long long *>(d_stage_);
+    a.num_ids = (long long)count;
+    a.err = d_err_;
+    if ((e = launch_zero_blocks(a, stream_)) != cudaSuccess) return device_error("zero_blocks", e);
+    return Status::Ok();
+}
+
+// zero_block (cpu.rs:151-160).
+Status B200Backend::zero_block(uint64_t block) {
+    Status s = validate_block(block);
+    if (!s.ok()) return s;
+    return launch_zero_ids(&block, 1);
+}
+
+Status B200Backend::zero_blocks(const uint64_t *blocks, uint64_t count) {
+    uint64_t valid = 0;
+    Status bad;
+    for (; valid < count; ++valid) {
+        bad = validate_block(blocks[valid]);
+        if (!bad.ok()) break;
+    }
+    Status s = launch_zero_ids(blocks, valid);
+    if (!s.ok()) return s;
+    return bad;
+}
+
+// ---------------------------------------------------------------------------
+// device entry points
+
+Status B200Backend::reshape_and_cache_dev(int64_t layer, const void *k, const void *v,
+                                          int64_t tok_stride, int64_t layer_stride,
+                                          const int64_t *slots, int64_t num_tokens, DType src,
+                                          cudaStream_t st) {
+    if (layer < -1 || (layer >= 0 && (uint64_t)layer >= cfg_.num_layers))
+        return error(PKV_ERR_INVALID_LAYER, layer, (int64_t)cfg_.num_layers,
+                     msg_layer((uint64_t)layer, cfg_.num_layers));
+    if (num_tokens < 0)
+        return error(PKV_ERR_SHAPE_MISMATCH, 0, num_tokens, "negative token count");
+    if (num_tokens == 0) return Status::Ok();
+    if (!k || !v || !slots) return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    if (static_cast<int>(src) < 0 || static_cast<int>(src) > 2)
+        return error(PKV_ERR_DEVICE, 0, 0, "unknown source dtype tag");
+    if (tok_stride <= 0) tok_stride = (int64_t)shard_entry_;
+    if ((uint64_t)tok_stride < shard_entry_)
+        return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)shard_entry_, tok_stride,
+                     "token stride shorter than an entry");
+    const bool all = layer == -1;
+    if (all && layer_stride <= 0) layer_stride = tok_stride * num_tokens;
+    if (all && layer_stride < tok_stride * num_tokens)
+        return error(PKV_ERR_SHAPE_MISMATCH, tok_stride * num_tokens, layer_stride,
+                     "layer stride shorter than a layer's rows");
+    DeviceGuard g(device_);
+    ReshapeLaunch a{};
+    a.k = k;
+    a.v = v;
+    a.src_token_stride = tok_stride;
+    a.src_layer_stride = all ? layer_stride : 0;
+    a.k_pool = k_plane_;
+    a.v_pool = v_plane_;
+    a.first_layer = all ? 0 : layer;
+    a.num_layers = all ? (long long)cfg_.num_layers : 1;
+    a.slots_per_layer = (long long)slots_per_layer();
+    a.entry_elems = (long long)shard_entry_;
+    a.slots = reinterpret_cast<const long long *>(slots);
+    a.num_tokens = num_tokens;
+    a.src_dtype = src;
+    a.pool_dtype = dtype_;
+    a.err = d_err_;
+    return check("reshape_and_cache", launch_reshape(a, sms_, st ? st : stream_));
+}
+
+Status B200Backend::copy_blocks_dev(const int64_t *pairs, int64_t count, cudaStream_t st) {
+    if (count < 0) return error(PKV_ERR_SHAPE_MISMATCH, 0, count, "negative pair count");
+    if (count == 0) return Status::Ok();
+    if (!pairs) return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    DeviceGuard g(device_);
+    CopyLaunch a{};
+    a.k_pool = k_plane_;
+    a.v_pool = v_plane_;
+    a.num_layers = (long long)cfg_.num_layers;
+    a.num_blocks = (long long)cfg_.num_blocks;
+    a.block_bytes = (long long)block_bytes();
+    a.pairs = reinterpret_cast<const long long *>(pairs);
+    a.num_pairs = count;
+    a.err = d_err_;
+    return check("copy_blocks", launch_copy_blocks(a, st ? st : stream_));
+}
+
+Status B200Backend::zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t st) {
+    if (count < 0) return error(PKV_ERR_SHAPE_MISMATCH, 0, count, "negative block count");
+    if (count == 0) return Status::Ok();
+    if (!blocks) return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    DeviceGuard g(device_);
+    ZeroLaunch a{};
+    a.k_pool = k_plane_;
+    a.v_pool = v_plane_;
+    a.num_layers = (long long)cfg_.num_layers;
+    a.num_blocks = (long long)cfg_.num_blocks;
+    a.block_bytes = (long long)block_bytes();
+    a.blocks = reinterpret_cast<const long long *>(blocks);
+    a.num_ids = count;
+    a.err = d_err_;
+    return check("zero_blocks", launch_zero_blocks(a, st ? st : stream_));
+}
+
+// Largest sequence count whose prefix fits in one CTA's shared memory.
+static constexpr int64_t kMaxResolveSeqs = 56 * 1024;
+
+Status B200Backend::resolve_slots_dev(const int32_t *tables, int64_t table_stride,
+                                      const int32_t *ctx, const int32_t *new_lens,
+                                      int64_t num_seqs, int64_t num_tokens, int32_t *cu,
+                                      int64_t *slots, cudaStream_t st) {
+    if (num_seqs < 0 || num_tokens < 0 || table_stride < 0)
+        return error(PKV_ERR_SHAPE_MISMATCH, 0, std::min({num_seqs, num_tokens, table_stride}),
+                     "negative size");
+    if (num_seqs > kMaxResolveSeqs)
+        return error(PKV_ERR_DEVICE, 0, 0,
+                     "slot resolution handles at most " + std::to_string(kMaxResolveSeqs) +
+                         " sequences per call");
+    if (num_tokens > std::numeric_limits<int32_t>::max())
+        return error(PKV_ERR_SHAPE_MISMATCH, std::numeric_limits<int32_t>::max(), num_tokens,
+                     "too many tokens for int32 cu_seqlens");
+    if (!cu || (num_seqs > 0 && (!ctx || !new_lens)) || (num_tokens > 0 && (!tables || !slots)))
+        return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    DeviceGuard g(device_);
+    ResolveLaunch a{};
+    a.tables = tables;
+    a.table_stride = table_stride;
+    a.ctx_lens = ctx;
+    a.new_lens = new_lens;
+    a.num_seqs = num_seqs;
+    a.num_tokens = num_tokens;
+    a.block_size = (long long)cfg_.block_size;
+    a.num_blocks = (long long)cfg_.num_blocks;
+    a.cu_seqlens = cu;
+    a.slots = reinterpret_cast<long long *>(slots);
+    a.err = d_err_;
+    return check("resolve_slots", launch_resolve_slots(a, sms_, st ? st : stream_));
+}
+
+Status B200Backend::digest(uint64_t *k, uint64_t *v, cudaStream_t st) {
+    DeviceGuard g(device_);
+    cudaStream_t s = st ? st : stream_;
+    unsigned long long host[2] = {0, 0};
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(d_digest_, 0, 2 * sizeof(unsigned long long), s)) != cudaSuccess)
+        return device_error("digest", e);
+    DigestLaunch a{};
+    a.k_pool = k_plane_;
+    a.v_pool = v_plane_;
+    a.rows = (long long)(cfg_.num_layers * slots_per_layer());
+    a.entry_elems = (long long)shard_entry_;
+    a.full_entry = (long long)full_entry_elems();
+    a.elem_offset = (long long)elem_offset();
+    a.pool_dtype = dtype_;
+    a.out = d_digest_;
+    if ((e = launch_digest(a, sms_, s)) != cudaSuccess) return device_error("digest", e);
+    if ((e = cudaMemcpyAsync(host, d_digest_, sizeof(host), cudaMemcpyDeviceToHost, s)) ||
+        (e = cudaStreamSynchronize(s)))
+        return device_error("digest", e);
+    *k = host[0];
+    *v = host[1];
+    return Status::Ok();
+}
+
+Status B200Backend::sync() {
+    DeviceGuard g(device_);
+    return check("cudaStreamSynchronize", cudaStreamSynchronize(stream_));
+}
+
+Status B200Backend::take_device_error(int64_t *index) {
+    DeviceGuard g(device_);
+    DevError h{};
+    cudaError_t e;
+    if ((e = cudaDeviceSynchronize()) || (e = cudaMemcpy(&h, d_err_, sizeof(h), cudaMemcpyDeviceToHost)) ||
+        (e = cudaMemset(d_err_, 0, sizeof(DevError))))
+        return ::pkv::device_error("reading the device error word", e);
+    if (index) *index = h.index;
+    if (h.code == PKV_OK) return Status::Ok();
+    return error(h.code, h.index, 0,
+                 "device entry point met a bad index at " + std::to_string(h.index));
+}
+
+}  // namespace pkv

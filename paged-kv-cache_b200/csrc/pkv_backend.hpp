@@ -1,0 +1,119 @@
+// pkv_backend.hpp -- B200Backend: the KvBackend trait of paged-kv-core
+// (crates/paged-kv-core/src/backend.rs:23-124) implemented over the sm_100a
+// kernels, with CpuBackend's validation order and error variants
+// (crates/paged-kv-core/src/cpu.rs:55-87) so that callers cannot tell the two
+// apart except by speed.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "pkv_b200.h"
+#include "pkv_internal.hpp"
+
+namespace pkv {
+
+// Result of one backend call: a pkv_status plus the CacheError variant's fields.
+struct Status {
+    int code = PKV_OK;
+    int64_t a = 0;
+    int64_t b = 0;
+    std::string msg;
+    bool ok() const { return code == PKV_OK; }
+    static Status Ok() { return {}; }
+};
+
+Status error(int code, int64_t a, int64_t b, std::string msg);
+Status device_error(const std::string &what, cudaError_t e);
+
+class B200Backend {
+   public:
+    static Status create(const pkv_config &cfg, DType dtype, int device, int shard_rank,
+                         int num_shards, std::unique_ptr<B200Backend> *out);
+    ~B200Backend();
+    B200Backend(const B200Backend &) = delete;
+    B200Backend &operator=(const B200Backend &) = delete;
+
+    // ---- KvBackend ----
+    const pkv_config &config() const { return cfg_; }
+    Status write_kv(uint64_t layer, pkv_slot dst, const void *k, uint64_t k_len, const void *v,
+                    uint64_t v_len, DType host);
+    Status write_kv_batch(uint64_t layer, const pkv_slot *dsts, uint64_t count, const void *k,
+                          uint64_t k_len, const void *v, uint64_t v_len, DType host);
+    Status read_kv(uint64_t layer, pkv_slot src, void *k_out, uint64_t k_len, void *v_out,
+                   uint64_t v_len, DType host);
+    Status copy_block(uint64_t src, uint64_t dst);
+    Status copy_blocks(const uint64_t *pairs, uint64_t count);
+    Status zero_block(uint64_t block);
+    Status zero_blocks(const uint64_t *blocks, uint64_t count);
+    uint64_t allocated_bytes() const;
+    std::string device_name() const;
+
+    // ---- device entry points ----
+    Status reshape_and_cache_dev(int64_t layer, const void *k, const void *v, int64_t tok_stride,
+                                 int64_t layer_stride, const int64_t *slots, int64_t num_tokens,
+                                 DType src, cudaStream_t s);
+    Status copy_blocks_dev(const int64_t *pairs, int64_t count, cudaStream_t s);
+    Status zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t s);
+    Status resolve_slots_dev(const int32_t *tables, int64_t table_stride, const int32_t *ctx,
+                             const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
+                             int32_t *cu, int64_t *slots, cudaStream_t s);
+    Status digest(uint64_t *k, uint64_t *v, cudaStream_t s);
+    Status sync();
+    Status take_device_error(int64_t *index);
+
+    // ---- geometry ----
+    uint64_t entry_elems() const { return shard_entry_; }
+    uint64_t full_entry_elems() const { return cfg_.num_kv_heads * cfg_.head_dim; }
+    uint64_t elem_offset() const { return shard_rank_ * shard_entry_; }
+    int shard_rank() const { return shard_rank_; }
+    int num_shards() const { return num_shards_; }
+    void *k_plane() const { return k_plane_; }
+    void *v_plane() const { return v_plane_; }
+    DType dtype() const { return dtype_; }
+    cudaStream_t stream() const { return stream_; }
+
+   private:
+    B200Backend() = default;
+
+    uint64_t slots_per_layer() const { return cfg_.num_blocks * cfg_.block_size; }
+    uint64_t entry_bytes() const { return shard_entry_ * dtype_size(dtype_); }
+    uint64_t block_bytes() const { return cfg_.block_size * entry_bytes(); }
+    Status validate_block(uint64_t block) const;
+    Status validate(uint64_t layer, pkv_slot at) const;
+    Status ensure_device_stage(size_t bytes);
+    Status ensure_host_stage(size_t bytes);
+    Status launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_t count, const void *k,
+                          const void *v, DType host);
+    Status launch_copy_pairs(const uint64_t *pairs, uint64_t count);
+    Status launch_zero_ids(const uint64_t *blocks, uint64_t count);
+    Status check(const char *what, cudaError_t e) const;
+
+    pkv_config cfg_{};
+    DType dtype_ = DType::F32;
+    int device_ = 0;
+    int sms_ = 148;
+    int shard_rank_ = 0;
+    int num_shards_ = 1;
+    uint64_t shard_entry_ = 0;
+    void *k_plane_ = nullptr;
+    void *v_plane_ = nullptr;
+    cudaStream_t stream_ = nullptr;
+    DevError *d_err_ = nullptr;
+    unsigned long long *d_digest_ = nullptr;
+    // Reused staging (the reference allocates fresh device buffers per call).
+    void *d_stage_ = nullptr;
+    size_t d_stage_bytes_ = 0;
+    void *h_stage_ = nullptr;  // pinned
+    size_t h_stage_bytes_ = 0;
+    cudaEvent_t h_stage_free_ = nullptr;  // last H2D out of h_stage_ has finished
+    cudaEvent_t inputs_consumed_ = nullptr;
+    std::vector<uint64_t> seen_;  // one bit per slot of a layer: duplicate detection
+    std::string gpu_name_;
+};
+
+}  // namespace pkv

@@ -1,0 +1,209 @@
+// pkv_capi.cpp -- the extern "C" surface declared in include/pkv_b200.h.
+// Each entry point records its status (code, the CacheError variant's fields
+// and a message) in thread-local storage and returns the code; no exception
+// crosses the boundary.
+
+#include <cstring>
+#include <exception>
+#include <new>
+
+#include "pkv_b200.h"
+#include "pkv_backend.hpp"
+
+struct pkv_backend {
+    std::unique_ptr<pkv::B200Backend> impl;
+};
+
+namespace {
+
+thread_local pkv::Status g_last;
+
+int finish(pkv::Status s) {
+    g_last = std::move(s);
+    return g_last.code;
+}
+
+int null_handle() { return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "null backend handle")); }
+
+bool valid_dtype(int t) { return t >= PKV_F32 && t <= PKV_F16; }
+
+int bad_dtype() { return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "unknown dtype tag")); }
+
+cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
+
+template <typename F>
+int guarded(F &&f) {
+    try {
+        return finish(f());
+    } catch (const std::bad_alloc &) {
+        return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "host out of memory"));
+    } catch (const std::exception &e) {
+        return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, e.what()));
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *pkv_last_error(void) { return g_last.msg.c_str(); }
+
+int pkv_last_error_fields(int64_t *field0, int64_t *field1) {
+    if (field0) *field0 = g_last.a;
+    if (field1) *field1 = g_last.b;
+    return g_last.code;
+}
+
+int pkv_create(const pkv_config *cfg, int dtype, int device, int shard_rank, int num_shards,
+               pkv_backend **out) {
+    if (!cfg || !out) return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "null argument"));
+    *out = nullptr;
+    if (!valid_dtype(dtype)) return bad_dtype();
+    return guarded([&] {
+        std::unique_ptr<pkv::B200Backend> impl;
+        pkv::Status s = pkv::B200Backend::create(*cfg, static_cast<pkv::DType>(dtype), device,
+                                                 shard_rank, num_shards, &impl);
+        if (s.ok()) *out = new pkv_backend{std::move(impl)};
+        return s;
+    });
+}
+
+int pkv_destroy(pkv_backend *b) {
+    delete b;
+    return finish(pkv::Status::Ok());
+}
+
+int pkv_get_config(const pkv_backend *b, pkv_config *out) {
+    if (!b || !out) return null_handle();
+    *out = b->impl->config();
+    return finish(pkv::Status::Ok());
+}
+
+uint64_t pkv_allocated_bytes(const pkv_backend *b) { return b ? b->impl->allocated_bytes() : 0; }
+
+int pkv_device_name(const pkv_backend *b, char *buf, uint64_t buf_len) {
+    if (!b || !buf || buf_len == 0) return null_handle();
+    const std::string n = b->impl->device_name();
+    const size_t m = std::min<size_t>(n.size(), buf_len - 1);
+    std::memcpy(buf, n.data(), m);
+    buf[m] = '\0';
+    return finish(pkv::Status::Ok());
+}
+
+int pkv_shard_info(const pkv_backend *b, int *rank, int *num_shards, uint64_t *elem_offset,
+                   uint64_t *shard_entry_elems) {
+    if (!b) return null_handle();
+    if (rank) *rank = b->impl->shard_rank();
+    if (num_shards) *num_shards = b->impl->num_shards();
+    if (elem_offset) *elem_offset = b->impl->elem_offset();
+    if (shard_entry_elems) *shard_entry_elems = b->impl->entry_elems();
+    return finish(pkv::Status::Ok());
+}
+
+int pkv_device_planes(const pkv_backend *b, void **k_plane, void **v_plane) {
+    if (!b) return null_handle();
+    if (k_plane) *k_plane = b->impl->k_plane();
+    if (v_plane) *v_plane = b->impl->v_plane();
+    return finish(pkv::Status::Ok());
+}
+
+int pkv_write_kv(pkv_backend *b, uint64_t layer, pkv_slot dst, const void *k, uint64_t k_len,
+                 const void *v, uint64_t v_len, int host_dtype) {
+    if (!b) return null_handle();
+    if (!valid_dtype(host_dtype)) return bad_dtype();
+    return guarded([&] {
+        return b->impl->write_kv(layer, dst, k, k_len, v, v_len, static_cast<pkv::DType>(host_dtype));
+    });
+}
+
+int pkv_write_kv_batch(pkv_backend *b, uint64_t layer, const pkv_slot *dsts, uint64_t count,
+                       const void *k, uint64_t k_len, const void *v, uint64_t v_len,
+                       int host_dtype) {
+    if (!b) return null_handle();
+    if (!valid_dtype(host_dtype)) return bad_dtype();
+    return guarded([&] {
+        return b->impl->write_kv_batch(layer, dsts, count, k, k_len, v, v_len,
+                                       static_cast<pkv::DType>(host_dtype));
+    });
+}
+
+int pkv_read_kv(pkv_backend *b, uint64_t layer, pkv_slot src, void *k_out, uint64_t k_len,
+                void *v_out, uint64_t v_len, int host_dtype) {
+    if (!b) return null_handle();
+    if (!valid_dtype(host_dtype)) return bad_dtype();
+    return guarded([&] {
+        return b->impl->read_kv(layer, src, k_out, k_len, v_out, v_len,
+                                static_cast<pkv::DType>(host_dtype));
+    });
+}
+
+int pkv_copy_block(pkv_backend *b, uint64_t src, uint64_t dst) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->copy_block(src, dst); });
+}
+
+int pkv_copy_blocks(pkv_backend *b, const uint64_t *pairs, uint64_t count) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->copy_blocks(pairs, count); });
+}
+
+int pkv_zero_block(pkv_backend *b, uint64_t block) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->zero_block(block); });
+}
+
+int pkv_zero_blocks(pkv_backend *b, const uint64_t *blocks, uint64_t count) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->zero_blocks(blocks, count); });
+}
+
+int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, const void *v,
+                              int64_t src_token_stride, int64_t src_layer_stride,
+                              const int64_t *slot_mapping, int64_t num_tokens, int src_dtype,
+                              void *stream) {
+    if (!b) return null_handle();
+    if (!valid_dtype(src_dtype)) return bad_dtype();
+    return guarded([&] {
+        return b->impl->reshape_and_cache_dev(layer, k, v, src_token_stride, src_layer_stride,
+                                              slot_mapping, num_tokens,
+                                              static_cast<pkv::DType>(src_dtype), as_stream(stream));
+    });
+}
+
+int pkv_copy_blocks_dev(pkv_backend *b, const int64_t *pairs, int64_t count, void *stream) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->copy_blocks_dev(pairs, count, as_stream(stream)); });
+}
+
+int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, void *stream) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->zero_blocks_dev(blocks, count, as_stream(stream)); });
+}
+
+int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t table_stride,
+                          const int32_t *ctx_lens, const int32_t *new_lens, int64_t num_seqs,
+                          int64_t num_tokens, int32_t *cu_seqlens, int64_t *slot_mapping,
+                          void *stream) {
+    if (!b) return null_handle();
+    return guarded([&] {
+        return b->impl->resolve_slots_dev(block_tables, table_stride, ctx_lens, new_lens, num_seqs,
+                                          num_tokens, cu_seqlens, slot_mapping, as_stream(stream));
+    });
+}
+
+int pkv_digest(pkv_backend *b, uint64_t *k_digest, uint64_t *v_digest, void *stream) {
+    if (!b || !k_digest || !v_digest) return null_handle();
+    return guarded([&] { return b->impl->digest(k_digest, v_digest, as_stream(stream)); });
+}
+
+int pkv_sync(pkv_backend *b) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->sync(); });
+}
+
+int pkv_device_error(pkv_backend *b, int64_t *index) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->take_device_error(index); });
+}
+
+}  // extern "C"

@@ -1,0 +1,99 @@
+// pkv_internal.hpp -- launch descriptors shared by the backend and the kernels.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace pkv {
+
+// Element type tags; values match pkv_dtype in include/pkv_b200.h.
+enum class DType : int { F32 = 0, BF16 = 1, F16 = 2 };
+
+inline int dtype_size(DType t) { return t == DType::F32 ? 4 : 2; }
+
+// First bad index met by a device entry point. `code` is a pkv_status;
+// `index` is the token / pair / block index it was met at.
+struct DevError {
+    int code;
+    int pad;
+    long long index;
+};
+
+// One reshape_and_cache launch: rows of `entry_elems` elements, read from
+// k/v (src_dtype) and scattered to the pool planes (pool_dtype) at
+// slot_mapping. Strides are in elements of the source type.
+struct ReshapeLaunch {
+    const void *k;
+    const void *v;
+    long long src_token_stride;
+    long long src_layer_stride;  // used when num_layers > 1
+    void *k_pool;                // plane base
+    void *v_pool;
+    long long first_layer;       // layer written by layer 0 of the source
+    long long num_layers;        // layers written by this launch
+    long long slots_per_layer;   // num_blocks * block_size
+    long long entry_elems;       // elements per entry held by this backend
+    const long long *slots;
+    long long num_tokens;
+    DType src_dtype;
+    DType pool_dtype;
+    DevError *err;
+};
+
+// Batched block copy over every layer and both planes; pairs is [num_pairs][2].
+struct CopyLaunch {
+    void *k_pool;
+    void *v_pool;
+    long long num_layers;
+    long long num_blocks;
+    long long block_bytes;  // block_size * entry_elems * elem size, one plane, one layer
+    const long long *pairs;
+    long long num_pairs;
+    DevError *err;
+};
+
+struct ZeroLaunch {
+    void *k_pool;
+    void *v_pool;
+    long long num_layers;
+    long long num_blocks;
+    long long block_bytes;
+    const long long *blocks;
+    long long num_ids;
+    DevError *err;
+};
+
+struct ResolveLaunch {
+    const int *tables;
+    long long table_stride;
+    const int *ctx_lens;
+    const int *new_lens;
+    long long num_seqs;
+    long long num_tokens;
+    long long block_size;
+    long long num_blocks;
+    int *cu_seqlens;
+    long long *slots;
+    DevError *err;
+};
+
+struct DigestLaunch {
+    const void *k_pool;
+    const void *v_pool;
+    long long rows;            // num_layers * num_blocks * block_size
+    long long entry_elems;     // per shard
+    long long full_entry;      // unsharded entry
+    long long elem_offset;     // this shard's offset in the full entry
+    DType pool_dtype;
+    unsigned long long *out;   // [2]: K digest, V digest (accumulated)
+};
+
+int num_sms(int device);
+
+cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t s);
+cudaError_t launch_copy_blocks(const CopyLaunch &a, cudaStream_t s);
+cudaError_t launch_zero_blocks(const ZeroLaunch &a, cudaStream_t s);
+cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t s);
+cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t s);
+
+}  // namespace pkv

@@ -1,0 +1,594 @@
+// pkv_kernels.cu -- sm_100a kernels of the paged KV cache data path.
+//
+// All four operations are pure data movement bounded by HBM bandwidth, so
+// the kernels are built around wide (16-byte) coalesced loads and stores,
+// several independent loads in flight per thread, streaming cache hints on
+// data that is touched once, and 64-bit address arithmetic throughout (a
+// 150 GB pool holds more than 2^31 elements per plane).
+//
+// Pool addressing is the reference's (crates/paged-kv-cuda/kernels/kernels.cu:11-14,
+// crates/paged-kv-core/src/cpu.rs:45-53):
+//   element (layer, block, slot, i) of a plane sits at
+//   ((layer*num_blocks + block)*block_size + slot)*entry + i
+// and, since block*block_size + slot is exactly the combined slot index s of
+// slot_mapping, at (layer*slots_per_layer + s)*entry + i.
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "pkv_internal.hpp"
+
+namespace pkv {
+namespace {
+
+constexpr int kThreads = 256;
+
+// pkv_status values recorded on the device.
+constexpr int kInvalidBlock = 2;
+constexpr int kSlotOutOfRange = 5;
+constexpr int kShapeMismatch = 6;
+
+__device__ __forceinline__ void record_error(DevError *e, int code, long long index) {
+    if (atomicCAS(&e->code, 0, code) == 0) e->index = index;
+}
+
+// ---- element conversion ---------------------------------------------------
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+
+template <typename D>
+__device__ __forceinline__ D from_f32(float f);
+template <>
+__device__ __forceinline__ float from_f32<float>(float f) { return f; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float f) { return __float2bfloat16_rn(f); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float f) { return __float2half_rn(f); }
+
+// ---- reshape_and_cache: same element type, byte copy ------------------------
+//
+// Work item = (token, vector of V within the entry). A thread resolves its
+// token's slot once and then moves its vector for every layer of its layer
+// chunk (blockIdx.y), UNROLL layers' K and V loads in flight at a time.
+// Consecutive threads cover consecutive vectors of one entry, so every warp
+// reads and writes whole contiguous runs.
+
+template <typename V, int UNROLL>
+__global__ void __launch_bounds__(kThreads)
+reshape_copy_kernel(const char *__restrict__ k, const char *__restrict__ v, long long src_tok,
+                    long long src_layer, char *__restrict__ kp, char *__restrict__ vp,
+                    long long pool_layer, const long long *__restrict__ slots, long long num_tokens,
+                    long long num_slots, int nvec, long long entry_bytes, int num_layers,
+                    int layers_per_chunk, DevError *err) {
+    const long long total = num_tokens * nvec;
+    const int l0 = blockIdx.y * layers_per_chunk;
+    const int l1 = min(num_layers, l0 + layers_per_chunk);
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x; it < total; it += stride) {
+        const long long t = it / nvec;
+        const int vec = (int)(it - t * nvec);
+        const long long s = __ldg(slots + t);
+        if (s < 0) continue;  // padding token
+        if (s >= num_slots) {
+            if (vec == 0 && blockIdx.y == 0) record_error(err, kInvalidBlock, t);
+            continue;
+        }
+        const long long col = (long long)vec * sizeof(V);
+        const char *ks = k + t * src_tok + l0 * src_layer + col;
+        const char *vs = v + t * src_tok + l0 * src_layer + col;
+        char *kd = kp + l0 * pool_layer + s * entry_bytes + col;
+        char *vd = vp + l0 * pool_layer + s * entry_bytes + col;
+        int l = l0;
+        for (; l + UNROLL <= l1; l += UNROLL) {
+            V kr[UNROLL], vr[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                kr[u] = __ldcs(reinterpret_cast<const V *>(ks + u * src_layer));
+                vr[u] = __ldcs(reinterpret_cast<const V *>(vs + u * src_layer));
+            }
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                __stcs(reinterpret_cast<V *>(kd + u * pool_layer), kr[u]);
+                __stcs(reinterpret_cast<V *>(vd + u * pool_layer), vr[u]);
+            }
+            ks += UNROLL * src_layer;
+            vs += UNROLL * src_layer;
+            kd += UNROLL * pool_layer;
+            vd += UNROLL * pool_layer;
+        }
+        for (; l < l1; ++l) {
+            const V kr = __ldcs(reinterpret_cast<const V *>(ks));
+            const V vr = __ldcs(reinterpret_cast<const V *>(vs));
+            __stcs(reinterpret_cast<V *>(kd), kr);
+            __stcs(reinterpret_cast<V *>(vd), vr);
+            ks += src_layer;
+            vs += src_layer;
+            kd += pool_layer;
+            vd += pool_layer;
+        }
+    }
+}
+
+// ---- reshape_and_cache with element conversion ------------------------------
+//
+// Work item = (token, group of PER elements). PER = 8 moves 16-byte vectors
+// of 16-bit types (and pairs of them for f32); PER = 1 is the fallback for
+// entries that are not a multiple of 8 elements or are misaligned.
+
+template <int BYTES>
+struct Raw {
+    uint4 q[BYTES / 16];
+};
+
+template <typename S, typename D, int PER>
+__global__ void __launch_bounds__(kThreads)
+reshape_convert_kernel(const S *__restrict__ k, const S *__restrict__ v, long long src_tok,
+                       long long src_layer, D *__restrict__ kp, D *__restrict__ vp,
+                       long long pool_layer, const long long *__restrict__ slots,
+                       long long num_tokens, long long num_slots, long long entry, int num_layers,
+                       int layers_per_chunk, DevError *err) {
+    const long long groups = entry / PER;
+    const long long total = num_tokens * groups;
+    const int l0 = blockIdx.y * layers_per_chunk;
+    const int l1 = min(num_layers, l0 + layers_per_chunk);
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x; it < total; it += stride) {
+        const long long t = it / groups;
+        const long long g = it - t * groups;
+        const long long s = __ldg(slots + t);
+        if (s < 0) continue;
+        if (s >= num_slots) {
+            if (g == 0 && blockIdx.y == 0) record_error(err, kInvalidBlock, t);
+            continue;
+        }
+        for (int l = l0; l < l1; ++l) {
+            const long long so = t * src_tok + l * src_layer + g * PER;
+            const long long dof = l * pool_layer + s * entry + g * PER;
+            if constexpr (PER == 8) {
+                Raw<8 * sizeof(S)> rk, rv;
+#pragma unroll
+                for (int q = 0; q < (int)(8 * sizeof(S) / 16); ++q) {
+                    rk.q[q] = __ldcs(reinterpret_cast<const uint4 *>(k + so) + q);
+                    rv.q[q] = __ldcs(reinterpret_cast<const uint4 *>(v + so) + q);
+                }
+                const S *ek = reinterpret_cast<const S *>(&rk);
+                const S *ev = reinterpret_cast<const S *>(&rv);
+                Raw<8 * sizeof(D)> wk, wv;
+                D *ok = reinterpret_cast<D *>(&wk);
+                D *ov = reinterpret_cast<D *>(&wv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    ok[e] = from_f32<D>(to_f32(ek[e]));
+                    ov[e] = from_f32<D>(to_f32(ev[e]));
+                }
+#pragma unroll
+                for (int q = 0; q < (int)(8 * sizeof(D) / 16); ++q) {
+                    __stcs(reinterpret_cast<uint4 *>(kp + dof) + q, wk.q[q]);
+                    __stcs(reinterpret_cast<uint4 *>(vp + dof) + q, wv.q[q]);
+                }
+            } else {
+                kp[dof] = from_f32<D>(to_f32(k[so]));
+                vp[dof] = from_f32<D>(to_f32(v[so]));
+            }
+        }
+    }
+}
+
+// ---- copy_blocks -------------------------------------------------------------
+//
+// One CTA per (pair, layer, plane, chunk of kThreads*UNROLL vectors); a
+// block's plane for one layer is block_size*entry contiguous elements, so
+// each CTA streams one contiguous run from src to dst.
+
+template <typename V, int UNROLL>
+__global__ void __launch_bounds__(kThreads)
+copy_blocks_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_layer,
+                   long long block_bytes, const long long *__restrict__ pairs, long long num_blocks,
+                   int num_layers, int chunks, DevError *err) {
+    long long x = blockIdx.x;
+    const int chunk = (int)(x % chunks);
+    x /= chunks;
+    const int plane = (int)(x & 1);
+    x >>= 1;
+    const int layer = (int)(x % num_layers);
+    const long long pair = x / num_layers;
+    const long long src = __ldg(pairs + 2 * pair);
+    const long long dst = __ldg(pairs + 2 * pair + 1);
+    if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {
+        if (threadIdx.x == 0 && chunk == 0 && plane == 0 && layer == 0)
+            record_error(err, kInvalidBlock, pair);
+        return;
+    }
+    if (src == dst) return;
+    char *base = (plane ? vp : kp) + layer * pool_layer;
+    const V *s = reinterpret_cast<const V *>(base + src * block_bytes);
+    V *d = reinterpret_cast<V *>(base + dst * block_bytes);
+    const long long nvec = block_bytes / (long long)sizeof(V);
+    const long long v0 = (long long)chunk * kThreads * UNROLL + threadIdx.x;
+    V r[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+        const long long i = v0 + (long long)u * kThreads;
+        if (i < nvec) r[u] = __ldcs(s + i);
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+        const long long i = v0 + (long long)u * kThreads;
+        if (i < nvec) __stcs(d + i, r[u]);
+    }
+}
+
+// ---- zero_blocks -------------------------------------------------------------
+
+template <typename V, int UNROLL>
+__global__ void __launch_bounds__(kThreads)
+zero_blocks_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_layer,
+                   long long block_bytes, const long long *__restrict__ ids, long long num_blocks,
+                   int num_layers, int chunks, DevError *err) {
+    long long x = blockIdx.x;
+    const int chunk = (int)(x % chunks);
+    x /= chunks;
+    const int plane = (int)(x & 1);
+    x >>= 1;
+    const int layer = (int)(x % num_layers);
+    const long long idx = x / num_layers;
+    const long long blk = __ldg(ids + idx);
+    if (blk < 0 || blk >= num_blocks) {
+        if (threadIdx.x == 0 && chunk == 0 && plane == 0 && layer == 0)
+            record_error(err, kInvalidBlock, idx);
+        return;
+    }
+    V *d = reinterpret_cast<V *>((plane ? vp : kp) + layer * pool_layer + blk * block_bytes);
+    const long long nvec = block_bytes / (long long)sizeof(V);
+    const long long v0 = (long long)chunk * kThreads * UNROLL + threadIdx.x;
+    V z;
+    memset(&z, 0, sizeof(V));
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+        const long long i = v0 + (long long)u * kThreads;
+        if (i < nvec) __stcs(d + i, z);
+    }
+}
+
+// ---- slot resolution -----------------------------------------------------------
+//
+// Every CTA scans new_lens into shared memory (exclusive prefix, one
+// contiguous segment per thread, then warp shuffles), so no CTA waits for
+// another; CTA 0 also publishes cu_seqlens. Each token then finds its
+// sequence by binary search over the prefix and applies
+// BlockTable::slot_for_position (block_table.rs:97-101).
+
+__device__ __forceinline__ int warp_inclusive_scan(int x) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    return x;
+}
+
+__global__ void __launch_bounds__(kThreads)
+resolve_slots_kernel(const int *__restrict__ tables, long long table_stride,
+                     const int *__restrict__ ctx, const int *__restrict__ nnew, int num_seqs,
+                     long long num_tokens, long long block_size, long long num_blocks,
+                     int *__restrict__ cu_out, long long *__restrict__ slots, DevError *err) {
+    extern __shared__ int s_cu[];  // num_seqs + 1
+    __shared__ int s_warp[kThreads / 32];
+    __shared__ int s_bad;
+    const int tid = threadIdx.x;
+    if (tid == 0) s_bad = 0;
+    __syncthreads();
+
+    // Per-thread segment sums.
+    const int seg = (num_seqs + kThreads - 1) / kThreads;
+    const int b0 = min(num_seqs, tid * seg);
+    const int b1 = min(num_seqs, b0 + seg);
+    int local = 0;
+    for (int q = b0; q < b1; ++q) {
+        const int n = __ldg(nnew + q);
+        if (n < 0 || __ldg(ctx + q) < 0) s_bad = 1;
+        local += max(n, 0);
+    }
+    // Block-wide exclusive scan of the segment sums.
+    const int incl = warp_inclusive_scan(local);
+    if ((tid & 31) == 31) s_warp[tid >> 5] = incl;
+    __syncthreads();
+    if (tid < 32) {
+        const int w = tid < kThreads / 32 ? s_warp[tid] : 0;
+        const int wi = warp_inclusive_scan(w);
+        if (tid < kThreads / 32) s_warp[tid] = wi - w;
+    }
+    __syncthreads();
+    int run = s_warp[tid >> 5] + incl - local;
+    for (int q = b0; q < b1; ++q) {
+        s_cu[q] = run;
+        run += max(__ldg(nnew + q), 0);
+    }
+    if (b1 == num_seqs && b0 < b1) s_cu[num_seqs] = run;
+    if (num_seqs == 0 && tid == 0) s_cu[0] = 0;
+    __syncthreads();
+
+    const long long total = s_cu[num_seqs];
+    if (blockIdx.x == 0) {
+        for (int q = tid; q <= num_seqs; q += kThreads) cu_out[q] = s_cu[q];
+        if (tid == 0) {
+            if (s_bad) record_error(err, kShapeMismatch, -1);
+            else if (total != num_tokens) record_error(err, kShapeMismatch, total);
+        }
+    }
+    if (s_bad || total != num_tokens) return;
+
+    const long long stride = (long long)gridDim.x * kThreads;
+    for (long long t = (long long)blockIdx.x * kThreads + tid; t < num_tokens; t += stride) {
+        int lo = 0, hi = num_seqs - 1;
+        while (lo < hi) {  // last q with s_cu[q] <= t; that sequence has new_lens > 0
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_cu[mid] <= t) lo = mid;
+            else hi = mid - 1;
+        }
+        const long long pos = (long long)__ldg(ctx + lo) + (t - s_cu[lo]);
+        const long long lb = pos / block_size;
+        const long long off = pos - lb * block_size;
+        long long out = -1;
+        if (lb < table_stride) {
+            const long long blk = __ldg(tables + (long long)lo * table_stride + lb);
+            if (blk >= 0 && blk < num_blocks) out = blk * block_size + off;
+            else record_error(err, kInvalidBlock, t);
+        } else {
+            record_error(err, kSlotOutOfRange, t);
+        }
+        slots[t] = out;
+    }
+}
+
+// ---- digest --------------------------------------------------------------------
+// splitmix64 finaliser (Steele, Lea & Flood, 2014) over (global index, bits).
+
+__device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ unsigned widen_bits(const float *p, long long i) { return __float_as_uint(p[i]); }
+__device__ __forceinline__ unsigned widen_bits(const __nv_bfloat16 *p, long long i) {
+    return (unsigned)(*reinterpret_cast<const unsigned short *>(p + i)) << 16;
+}
+__device__ __forceinline__ unsigned widen_bits(const __half *p, long long i) {
+    return __float_as_uint(__half2float(p[i]));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+digest_kernel(const T *__restrict__ kp, const T *__restrict__ vp, long long rows, long long entry,
+              long long full_entry, long long elem_offset, unsigned long long *out) {
+    const int plane = blockIdx.y;
+    const T *p = plane ? vp : kp;
+    const long long total = rows * entry;
+    unsigned long long acc = 0;
+    const long long stride = (long long)gridDim.x * kThreads;
+    for (long long i = (long long)blockIdx.x * kThreads + threadIdx.x; i < total; i += stride) {
+        const unsigned bits = widen_bits(p, i);
+        if (bits == 0) continue;
+        const long long r = i / entry;
+        const long long gidx = r * full_entry + elem_offset + (i - r * entry);
+        acc += mix64(((unsigned long long)gidx * 2 + plane) * 0x9E3779B97F4A7C15ull + bits);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0 && acc) atomicAdd(out + plane, acc);
+}
+
+// ---- helpers ---------------------------------------------------------------------
+
+inline bool aligned(const void *p, long long a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+template <typename S, typename D>
+cudaError_t launch_convert(const ReshapeLaunch &a, dim3 grid_chunks, int layers_per_chunk,
+                           bool per8, int sms, cudaStream_t st) {
+    const long long per = per8 ? 8 : 1;
+    const long long total = a.num_tokens * (a.entry_elems / per);
+    long long bx = std::min<long long>((total + kThreads - 1) / kThreads, (long long)sms * 64);
+    dim3 grid((unsigned)std::max<long long>(bx, 1), grid_chunks.y);
+    const long long pool_layer = a.slots_per_layer * a.entry_elems;
+    D *kp = static_cast<D *>(a.k_pool) + a.first_layer * pool_layer;
+    D *vp = static_cast<D *>(a.v_pool) + a.first_layer * pool_layer;
+    if (per8)
+        reshape_convert_kernel<S, D, 8><<<grid, kThreads, 0, st>>>(
+            static_cast<const S *>(a.k), static_cast<const S *>(a.v), a.src_token_stride,
+            a.src_layer_stride, kp, vp, pool_layer, a.slots, a.num_tokens, a.slots_per_layer,
+            a.entry_elems, (int)a.num_layers, layers_per_chunk, a.err);
+    else
+        reshape_convert_kernel<S, D, 1><<<grid, kThreads, 0, st>>>(
+            static_cast<const S *>(a.k), static_cast<const S *>(a.v), a.src_token_stride,
+            a.src_layer_stride, kp, vp, pool_layer, a.slots, a.num_tokens, a.slots_per_layer,
+            a.entry_elems, (int)a.num_layers, layers_per_chunk, a.err);
+    return cudaGetLastError();
+}
+
+template <typename S>
+cudaError_t launch_convert_from(const ReshapeLaunch &a, dim3 g, int lpc, bool per8, int sms,
+                                cudaStream_t st) {
+    switch (a.pool_dtype) {
+        case DType::F32: return launch_convert<S, float>(a, g, lpc, per8, sms, st);
+        case DType::BF16: return launch_convert<S, __nv_bfloat16>(a, g, lpc, per8, sms, st);
+        case DType::F16: return launch_convert<S, __half>(a, g, lpc, per8, sms, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <typename V>
+cudaError_t launch_copy_v(const ReshapeLaunch &a, long long entry_bytes, int layers_per_chunk,
+                          int chunks_y, int sms, cudaStream_t st) {
+    const int es = dtype_size(a.pool_dtype);
+    const int nvec = (int)(entry_bytes / (long long)sizeof(V));
+    const long long total = a.num_tokens * nvec;
+    // Enough CTAs to cover every item once, up to a cap past which threads loop.
+    long long bx = std::min<long long>((total + kThreads - 1) / kThreads, (long long)sms * 256);
+    dim3 grid((unsigned)std::max<long long>(bx, 1), (unsigned)chunks_y);
+    const long long pool_layer = a.slots_per_layer * entry_bytes;
+    char *kp = static_cast<char *>(a.k_pool) + a.first_layer * pool_layer;
+    char *vp = static_cast<char *>(a.v_pool) + a.first_layer * pool_layer;
+    reshape_copy_kernel<V, 4><<<grid, kThreads, 0, st>>>(
+        static_cast<const char *>(a.k), static_cast<const char *>(a.v), a.src_token_stride * es,
+        a.src_layer_stride * es, kp, vp, pool_layer, a.slots, a.num_tokens, a.slots_per_layer,
+        nvec, entry_bytes, (int)a.num_layers, layers_per_chunk, a.err);
+    return cudaGetLastError();
+}
+
+// Largest power-of-two vector width (<= 16 bytes) dividing every byte offset.
+int pick_vector_bytes(long long elem_bytes, std::initializer_list<long long> byte_quantities,
+                      std::initializer_list<const void *> ptrs) {
+    int vb = 16;
+    while (vb > elem_bytes) {
+        bool ok = true;
+        for (long long q : byte_quantities) ok = ok && (q % vb == 0);
+        for (const void *p : ptrs) ok = ok && aligned(p, vb);
+        if (ok) break;
+        vb /= 2;
+    }
+    return vb;
+}
+
+}  // namespace
+
+int num_sms(int device) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+        n = 148;
+    return n;
+}
+
+cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t st) {
+    if (a.num_tokens <= 0 || a.num_layers <= 0 || a.entry_elems <= 0) return cudaSuccess;
+    const int es = dtype_size(a.pool_dtype);
+    const long long entry_bytes = a.entry_elems * es;
+    // Split layers into chunks (grid.y) only when tokens alone cannot fill the GPU.
+    const long long items = a.num_tokens * std::max<long long>(1, entry_bytes / 16);
+    const long long want = (long long)sms * 2048 * 2;
+    long long chunks = std::min<long long>(a.num_layers, std::max<long long>(1, want / std::max<long long>(items, 1)));
+    const int lpc = (int)((a.num_layers + chunks - 1) / chunks);
+    chunks = (a.num_layers + lpc - 1) / lpc;
+
+    if (a.src_dtype == a.pool_dtype) {
+        const int vb = pick_vector_bytes(
+            es, {entry_bytes, a.src_token_stride * es, a.num_layers > 1 ? a.src_layer_stride * es : 0},
+            {a.k, a.v});
+        switch (vb) {
+            case 16: return launch_copy_v<uint4>(a, entry_bytes, lpc, (int)chunks, sms, st);
+            case 8: return launch_copy_v<uint2>(a, entry_bytes, lpc, (int)chunks, sms, st);
+            case 4: return launch_copy_v<unsigned int>(a, entry_bytes, lpc, (int)chunks, sms, st);
+            default: return launch_copy_v<unsigned short>(a, entry_bytes, lpc, (int)chunks, sms, st);
+        }
+    }
+    const int ss = dtype_size(a.src_dtype);
+    const bool per8 = a.entry_elems % 8 == 0 && a.src_token_stride % 8 == 0 &&
+                      (a.num_layers == 1 || a.src_layer_stride % 8 == 0) && aligned(a.k, 16) &&
+                      aligned(a.v, 16) && ss * 8 % 16 == 0;
+    dim3 g(1, (unsigned)chunks);
+    switch (a.src_dtype) {
+        case DType::F32: return launch_convert_from<float>(a, g, lpc, per8, sms, st);
+        case DType::BF16: return launch_convert_from<__nv_bfloat16>(a, g, lpc, per8, sms, st);
+        case DType::F16: return launch_convert_from<__half>(a, g, lpc, per8, sms, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+namespace {
+template <typename V>
+cudaError_t copy_v(const CopyLaunch &a, cudaStream_t st) {
+    constexpr int U = 4;
+    const long long nvec = a.block_bytes / (long long)sizeof(V);
+    const int chunks = (int)((nvec + kThreads * U - 1) / (kThreads * U));
+    const long long grid = a.num_pairs * a.num_layers * 2 * chunks;
+    copy_blocks_kernel<V, U><<<(unsigned)grid, kThreads, 0, st>>>(
+        static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool),
+        a.num_blocks * a.block_bytes, a.block_bytes, a.pairs, a.num_blocks, (int)a.num_layers,
+        chunks, a.err);
+    return cudaGetLastError();
+}
+template <typename V>
+cudaError_t zero_v(const ZeroLaunch &a, cudaStream_t st) {
+    constexpr int U = 4;
+    const long long nvec = a.block_bytes / (long long)sizeof(V);
+    const int chunks = (int)((nvec + kThreads * U - 1) / (kThreads * U));
+    const long long grid = a.num_ids * a.num_layers * 2 * chunks;
+    zero_blocks_kernel<V, U><<<(unsigned)grid, kThreads, 0, st>>>(
+        static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool),
+        a.num_blocks * a.block_bytes, a.block_bytes, a.blocks, a.num_blocks, (int)a.num_layers,
+        chunks, a.err);
+    return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_copy_blocks(const CopyLaunch &a, cudaStream_t st) {
+    if (a.num_pairs <= 0 || a.num_layers <= 0 || a.block_bytes <= 0) return cudaSuccess;
+    const int vb = pick_vector_bytes(2, {a.block_bytes}, {a.k_pool, a.v_pool});
+    switch (vb) {
+        case 16: return copy_v<uint4>(a, st);
+        case 8: return copy_v<uint2>(a, st);
+        case 4: return copy_v<unsigned int>(a, st);
+        default: return copy_v<unsigned short>(a, st);
+    }
+}
+
+cudaError_t launch_zero_blocks(const ZeroLaunch &a, cudaStream_t st) {
+    if (a.num_ids <= 0 || a.num_layers <= 0 || a.block_bytes <= 0) return cudaSuccess;
+    const int vb = pick_vector_bytes(2, {a.block_bytes}, {a.k_pool, a.v_pool});
+    switch (vb) {
+        case 16: return zero_v<uint4>(a, st);
+        case 8: return zero_v<uint2>(a, st);
+        case 4: return zero_v<unsigned int>(a, st);
+        default: return zero_v<unsigned short>(a, st);
+    }
+}
+
+cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t st) {
+    const size_t smem = (size_t)(a.num_seqs + 1) * sizeof(int);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(resolve_slots_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    long long bx = std::min<long long>((a.num_tokens + kThreads - 1) / kThreads, (long long)sms * 4);
+    bx = std::max<long long>(bx, 1);
+    resolve_slots_kernel<<<(unsigned)bx, kThreads, smem, st>>>(
+        a.tables, a.table_stride, a.ctx_lens, a.new_lens, (int)a.num_seqs, a.num_tokens,
+        a.block_size, a.num_blocks, a.cu_seqlens, a.slots, a.err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t st) {
+    const long long total = a.rows * a.entry_elems;
+    if (total <= 0) return cudaSuccess;
+    long long bx = std::min<long long>((total + kThreads - 1) / kThreads, (long long)sms * 16);
+    dim3 grid((unsigned)std::max<long long>(bx, 1), 2);
+    switch (a.pool_dtype) {
+        case DType::F32:
+            digest_kernel<float><<<grid, kThreads, 0, st>>>(
+                static_cast<const float *>(a.k_pool), static_cast<const float *>(a.v_pool), a.rows,
+                a.entry_elems, a.full_entry, a.elem_offset, a.out);
+            break;
+        case DType::BF16:
+            digest_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(
+                static_cast<const __nv_bfloat16 *>(a.k_pool),
+                static_cast<const __nv_bfloat16 *>(a.v_pool), a.rows, a.entry_elems, a.full_entry,
+                a.elem_offset, a.out);
+            break;
+        case DType::F16:
+            digest_kernel<__half><<<grid, kThreads, 0, st>>>(
+                static_cast<const __half *>(a.k_pool), static_cast<const __half *>(a.v_pool),
+                a.rows, a.entry_elems, a.full_entry, a.elem_offset, a.out);
+            break;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace pkv

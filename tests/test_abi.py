@@ -1,0 +1,81 @@
+"""The C-ABI library loads, exports every symbol its headers declare, and
+fails loudly (no CPU fallback) where there is no GPU. No compute calls."""
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_functions():
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"\b(pkv_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    from pagedkv import _lib
+
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(_lib.lib, n)]
+    assert not missing, missing
+
+
+def test_every_declared_symbol_has_a_prototype():
+    from pagedkv import _lib
+
+    assert set(declared_functions()) <= set(_lib._PROTOS)
+
+
+def test_status_codes_map_to_cache_error_variants():
+    from pagedkv import errors as E
+
+    assert E.from_status(7, 99, 2, "") == E.InvalidLayer(99, 2)
+    assert E.from_status(2, 99, 8, "") == E.InvalidBlock(99, 8)
+    assert E.from_status(5, 99, 4, "") == E.SlotOutOfRange(99, 4)
+    assert E.from_status(6, 8, 7, "") == E.ShapeMismatch(8, 7)
+    assert E.from_status(9, 0, 0, "boom") == E.Device("boom")
+    assert E.InvalidLayer(1, 2) != E.InvalidBlock(1, 2)
+
+
+def test_null_handle_is_a_device_error_not_a_crash():
+    from pagedkv import _lib
+
+    assert _lib.lib.pkv_sync(None) == 9
+    code, _, _, msg = _lib.last_error()
+    assert code == 9 and "null" in msg
+
+
+def test_unknown_dtype_tag_is_rejected_before_any_device_work():
+    from pagedkv import _lib
+
+    cfg = _lib.Config(8, 4, 2, 4, 2, 4)
+    h = C.c_void_p()
+    assert _lib.lib.pkv_create(C.byref(cfg), 7, 0, 0, 1, C.byref(h)) == 9
+    assert h.value is None
+
+
+def test_create_without_a_gpu_fails_loudly():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from pagedkv import B200Backend, CacheConfig, Device
+
+    with pytest.raises(Device):
+        B200Backend(CacheConfig.tiny(8))
+
+
+def test_config_errors_are_reported_before_device_work():
+    from pagedkv import B200Backend, CacheConfig, Device
+
+    with pytest.raises(Device, match="dtype_bytes"):
+        B200Backend(CacheConfig.tiny(8), dtype="bf16")  # tiny says 4 bytes per element
+    with pytest.raises(Device, match="shard"):
+        B200Backend(CacheConfig.tiny(8), shard_rank=0, num_shards=3)  # 8 elements / 3
