@@ -51,8 +51,14 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-ops", action="store_true")
     p.add_argument("--profile-small", action="store_true",
-                   help="one small step of each kernel, for ncu captures")
-    return p.parse_args()
+                   help="an 8,192-token chunk over a 2,048-block pool and nothing else, "
+                        "for ncu captures")
+    a = p.parse_args()
+    a.chunk_tokens, a.chunk_prompts, a.chunk_blocks = CHUNK_TOKENS, CHUNK_PROMPTS, BLOCKS_PER_CHUNK
+    if a.profile_small:
+        a.chunk_tokens, a.chunk_prompts, a.chunk_blocks = 8192, 16, 2048
+        a.no_e2e = a.no_cpu = a.no_ops = True
+    return a
 
 
 # ---- clocks ---------------------------------------------------------------------------------
@@ -136,21 +142,22 @@ def profile_traffic(name: str):
 # ---- workload ---------------------------------------------------------------------------------
 
 
-def build_batch(world: int):
+def build_batch(world: int, tokens: int = CHUNK_TOKENS, prompts: int = CHUNK_PROMPTS,
+                blocks: int = BLOCKS_PER_CHUNK):
     """N prefill chunks, chunk c drawing its blocks from its own shuffled
-    32,768-block range of the pool."""
+    `blocks`-block range of the pool."""
     import numpy as np
 
     from pagedkv import CacheConfig
     from pagedkv.workloads import prefill_chunk
 
-    cfg = CacheConfig(num_blocks=BLOCKS_PER_CHUNK * world, **GEOM)
-    one = CacheConfig(num_blocks=BLOCKS_PER_CHUNK, **GEOM)
+    cfg = CacheConfig(num_blocks=blocks * world, **GEOM)
+    one = CacheConfig(num_blocks=blocks, **GEOM)
     ctx, new, tabs = [], [], []
     for c in range(world):
-        b = prefill_chunk(seed=c, num_prompts=CHUNK_PROMPTS, budget=CHUNK_TOKENS, cfg=one)
+        b = prefill_chunk(seed=c, num_prompts=prompts, budget=tokens, cfg=one)
         t = b.tables.astype(np.int64)
-        t[t >= 0] += c * BLOCKS_PER_CHUNK
+        t[t >= 0] += c * blocks
         ctx.append(b.ctx)
         new.append(b.new)
         tabs.append(t.astype(np.int32))
@@ -209,7 +216,8 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    cfg, tables, ctx, new = build_batch(world)
+    cfg, tables, ctx, new = build_batch(world, args.chunk_tokens, args.chunk_prompts,
+                                        args.chunk_blocks)
     T = int(new.sum())
     S = len(new)
     backend = B200Backend(cfg, dtype="bf16", device=local, shard_rank=rank, num_shards=world)
@@ -287,7 +295,7 @@ def run_ours(args):
         "dtype": "bf16",
         "data": "synthetic (seeded: log-uniform prompt lengths, shuffled free list, normal K/V)",
         "config": {
-            "workload": f"ragged prefill chunk x{world}: {world}x{CHUNK_TOKENS} tokens "
+            "workload": f"ragged prefill chunk x{world}: {world}x{args.chunk_tokens} tokens "
                         f"({S} prompts, log-uniform 128..4096), Qwen2-7B KV geometry "
                         f"(28 layers, 4 KV heads x 128, bs 16), pool {cfg.num_blocks} blocks "
                         f"head-sharded {world} ways; step = device slot resolution + "

@@ -29,6 +29,8 @@ struct Status {
 
 Status error(int code, int64_t a, int64_t b, std::string msg);
 Status device_error(const std::string &what, cudaError_t e);
+// Stores `s` as this thread's last status (pkv_last_error*) and returns its code.
+int finish(Status s);
 
 class B200Backend {
    public:

@@ -15,13 +15,18 @@ struct pkv_backend {
 };
 
 namespace {
-
 thread_local pkv::Status g_last;
+}  // namespace
 
-int finish(pkv::Status s) {
+// Records the status of the C-ABI call that is returning on this thread.
+int pkv::finish(pkv::Status s) {
     g_last = std::move(s);
     return g_last.code;
 }
+
+using pkv::finish;
+
+namespace {
 
 int null_handle() { return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "null backend handle")); }
 
