@@ -147,11 +147,12 @@ def test_scheduler_traces_match_oracle(seed):
     """Poisson arrivals, log-uniform prompts, geometric outputs, occasional
     forks, a tight pool: every step's outcome must agree exactly."""
     st = Stream(100 + seed)
-    nb, bs, mb = 64, 4, 6
+    nb, bs, mb = 32, 4, 8
     mine, ref = Scheduler(nb, bs, mb), H.Scheduler(nb, bs, mb)
     sid = 0
+    preempted = 0
     for _ in range(300):
-        for _ in range(int(st.poisson(1, 0.7)[0])):
+        for _ in range(int(st.poisson(1, 1.0)[0])):
             p = int(st.log_uniform_int(1, 1, 40)[0])
             g = int(st.geometric(1, 6.0)[0])
             try:
@@ -174,8 +175,10 @@ def test_scheduler_traces_match_oracle(seed):
         assert [(d.id, (d.slot.block, d.slot.slot), d.cow) for d in g.decoded] == \
             [(d[0], d[1], d[2]) for d in e.decoded]
         assert g.preempted == e.preempted and g.finished == e.finished
+        preempted += len(g.preempted)
         assert set(g.freed) == {b for b in range(nb) if ref.allocator.ref_counts[b] == 0} & set(g.freed)
         assert mine.num_running() == len(ref.running) and mine.num_waiting() == len(ref.waiting)
+    assert preempted > 0  # the trace exercises recompute preemption
     ids, tok, gen, tab = mine.running(table_stride=nb)
     assert [int(x) for x in ids] == [r.id for r in ref.running]
     for row, r in zip(tab, ref.running):
