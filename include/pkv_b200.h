@@ -21,8 +21,9 @@
  * items before a failing item in place.
  *
  * Threading: one backend handle is used by one host thread at a time (the
- * trait's mutating methods take &mut self). Work is issued on the handle's
- * own CUDA stream unless a device entry point is given another one.
+ * trait's mutating methods take &mut self). Host-buffer methods issue their
+ * work on the handle's own blocking CUDA stream, which is ordered with the
+ * legacy default stream; device entry points use the stream they are given.
  */
 #ifndef PKV_B200_H
 #define PKV_B200_H
@@ -135,9 +136,9 @@ int pkv_zero_block(pkv_backend *b, uint64_t block);
 int pkv_zero_blocks(pkv_backend *b, const uint64_t *blocks, uint64_t count);
 
 /* ---- device entry points (inputs already in device memory) ----------------
- * stream: a cudaStream_t, or NULL for the backend's own stream. These do not
- * synchronise. Bad indices found on the device are skipped and recorded in
- * the backend's device error word (pkv_device_error). */
+ * stream: a cudaStream_t; NULL is the legacy default stream, as everywhere in
+ * CUDA. These do not synchronise. Bad indices found on the device are skipped
+ * and recorded in the backend's device error word (pkv_device_error). */
 
 /* reshape_and_cache (crates/paged-kv-cuda/kernels/kernels.cu:31-60).
  * layer >= 0: k, v are [num_tokens][entry] rows (row pitch src_token_stride

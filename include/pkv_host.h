@@ -41,7 +41,7 @@ uint64_t pkv_table_num_tokens(const pkv_table *t);
 uint64_t pkv_table_num_blocks(const pkv_table *t);
 /* Copies up to cap block ids; returns the table's block count. */
 uint64_t pkv_table_blocks(const pkv_table *t, uint32_t *out, uint64_t cap);
-/* append (:135-160): slot written to *block/*slot; *cow = 1 with *cow_src,
+/* append (:135-160): the slot goes to *block and *slot; *cow = 1 with *cow_src,
  * *cow_dst when the shared tail was made private. */
 int pkv_table_append(pkv_table *t, pkv_allocator *a, uint32_t *block, uint64_t *slot, int *cow,
                      uint32_t *cow_src, uint32_t *cow_dst);

@@ -138,7 +138,9 @@ Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int s
         return device_error("cudaGetDeviceProperties", e);
     b->gpu_name_ = prop.name;
     b->sms_ = num_sms(device);
-    if ((e = cudaStreamCreateWithFlags(&b->stream_, cudaStreamNonBlocking)) != cudaSuccess)
+    // A blocking stream: host-buffer calls stay ordered with work that callers
+    // issue on the legacy default stream.
+    if ((e = cudaStreamCreateWithFlags(&b->stream_, cudaStreamDefault)) != cudaSuccess)
         return device_error("cudaStreamCreate", e);
     if ((e = cudaEventCreateWithFlags(&b->h_stage_free_, cudaEventDisableTiming)) != cudaSuccess ||
         (e = cudaEventCreateWithFlags(&b->inputs_consumed_, cudaEventDisableTiming)) != cudaSuccess)
@@ -554,7 +556,7 @@ Status B200Backend::reshape_and_cache_dev(int64_t layer, const void *k, const vo
     a.src_dtype = src;
     a.pool_dtype = dtype_;
     a.err = d_err_;
-    return check("reshape_and_cache", launch_reshape(a, sms_, st ? st : stream_));
+    return check("reshape_and_cache", launch_reshape(a, sms_, st));
 }
 
 Status B200Backend::copy_blocks_dev(const int64_t *pairs, int64_t count, cudaStream_t st) {
@@ -571,7 +573,7 @@ Status B200Backend::copy_blocks_dev(const int64_t *pairs, int64_t count, cudaStr
     a.pairs = reinterpret_cast<const long long *>(pairs);
     a.num_pairs = count;
     a.err = d_err_;
-    return check("copy_blocks", launch_copy_blocks(a, st ? st : stream_));
+    return check("copy_blocks", launch_copy_blocks(a, st));
 }
 
 Status B200Backend::zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t st) {
@@ -588,7 +590,7 @@ Status B200Backend::zero_blocks_dev(const int64_t *blocks, int64_t count, cudaSt
     a.blocks = reinterpret_cast<const long long *>(blocks);
     a.num_ids = count;
     a.err = d_err_;
-    return check("zero_blocks", launch_zero_blocks(a, st ? st : stream_));
+    return check("zero_blocks", launch_zero_blocks(a, st));
 }
 
 // Largest sequence count whose prefix fits in one CTA's shared memory.
@@ -623,12 +625,12 @@ Status B200Backend::resolve_slots_dev(const int32_t *tables, int64_t table_strid
     a.cu_seqlens = cu;
     a.slots = reinterpret_cast<long long *>(slots);
     a.err = d_err_;
-    return check("resolve_slots", launch_resolve_slots(a, sms_, st ? st : stream_));
+    return check("resolve_slots", launch_resolve_slots(a, sms_, st));
 }
 
 Status B200Backend::digest(uint64_t *k, uint64_t *v, cudaStream_t st) {
     DeviceGuard g(device_);
-    cudaStream_t s = st ? st : stream_;
+    cudaStream_t s = st;
     unsigned long long host[2] = {0, 0};
     cudaError_t e;
     if ((e = cudaMemsetAsync(d_digest_, 0, 2 * sizeof(unsigned long long), s)) != cudaSuccess)

@@ -62,8 +62,11 @@ def _ptr(t) -> int:
 
 
 def _stream_ptr(stream) -> int | None:
+    """cudaStream_t for a device entry point: torch's current stream by default."""
     if stream is None:
-        return None
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream or None
     if isinstance(stream, int):
         return stream
     return stream.cuda_stream
