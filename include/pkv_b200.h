@@ -175,6 +175,40 @@ int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t t
  * (mod 2^64) to the digest of the whole pool. Synchronous. */
 int pkv_digest(pkv_backend *b, uint64_t *k_digest, uint64_t *v_digest, void *stream);
 
+/* Slot resolution + reshape_and_cache that allocates nothing. No counterpart
+ * in the reference.
+ *
+ * For callers that cannot call cudaMalloc: for example a plugin running
+ * inside an inference engine that has already reserved (nearly) all HBM for
+ * its own memory pool and hands out only the buffers it owns. The caller
+ * passes every input and output, including the pool planes (laid out as a
+ * backend created with the same config, dtype and shard would lay them out)
+ * and cu_seqlens[num_seqs + 1]; the intermediate slot mapping and the device
+ * error word live in a fixed static device array of
+ * PKV_NOALLOC_SCRATCH_BYTES, which every GPU that loads the library holds
+ * until the process exits. Results are those of pkv_resolve_slots_dev
+ * followed by pkv_reshape_and_cache_dev.
+ *
+ * - num_tokens above PKV_NOALLOC_MAX_TOKENS is rejected (ShapeMismatch{max,
+ *   num_tokens}) before any device work.
+ * - Runs on the current device; the first call on a device looks up the
+ *   scratch array's device address, so make that first call before any
+ *   stream capture.
+ * - All calls on a device share the scratch array: calls whose work overlaps
+ *   on the GPU race. Each call clears what it needs before use.
+ * - device_status (optional, device memory, 2 x int64) receives {status,
+ *   index} of the first bad index met on the device (0 = none). */
+#define PKV_NOALLOC_MAX_TOKENS 131072
+#define PKV_NOALLOC_SCRATCH_BYTES (256 + 8 * PKV_NOALLOC_MAX_TOKENS)
+int pkv_resolve_and_cache_noalloc(const pkv_config *cfg, int pool_dtype, int shard_rank,
+                                  int num_shards, void *k_plane, void *v_plane,
+                                  const int32_t *block_tables, int64_t table_stride,
+                                  const int32_t *ctx_lens, const int32_t *new_lens,
+                                  int64_t num_seqs, int64_t num_tokens, int32_t *cu_seqlens,
+                                  int64_t layer, const void *k, const void *v,
+                                  int64_t src_token_stride, int64_t src_layer_stride,
+                                  int src_dtype, int64_t *device_status, void *stream);
+
 /* Wait for all work issued on the backend's stream. */
 int pkv_sync(pkv_backend *b);
 /* Synchronise, then read and clear the device error word. Returns PKV_OK if no
