@@ -288,6 +288,15 @@ def run_ours(args):
     reshape_avg = max_over_ranks(sum(reshape_ms) / K)
     resolve_avg = max_over_ranks(sum(resolve_ms) / K)
 
+    # Shard verification: each rank digests its shard and the rows it wrote;
+    # the ranks all-gather the digests (NCCL) and check them.
+    from pagedkv.shard import verify_over_group
+
+    verify = verify_over_group(backend.digest(stream=stream),
+                               backend.digest_rows(k, v, d_slots, stream=stream), device=dev)
+    if not verify["ok"]:
+        raise SystemExit(f"bench: shard verification failed: {verify}")
+
     tokens_all = T * world
     value = tokens_all * K / (total_ms / 1e3)
     eb = es * 2
@@ -337,6 +346,7 @@ def run_ours(args):
         },
         "resolve_slots_ms": resolve_avg,
         "gpu_launches": 2 * K,
+        "verify": verify,
         "clocks": {**clocks.summary(),
                    "window": "sampled every 200 ms over 1.3 s of continuous load around the timed steps"},
     }

@@ -175,6 +175,16 @@ int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t t
  * (mod 2^64) to the digest of the whole pool. Synchronous. */
 int pkv_digest(pkv_backend *b, uint64_t *k_digest, uint64_t *v_digest, void *stream);
 
+/* Digests (as pkv_digest) that this backend's planes would have if the given
+ * rows (arguments as pkv_reshape_and_cache_dev; negative slots skipped) had
+ * been written into an all-zero pool. With distinct slots, comparing this to
+ * pkv_digest after the write verifies the pool without reading it back.
+ * Synchronous. */
+int pkv_digest_rows_dev(pkv_backend *b, int64_t layer, const void *k, const void *v,
+                        int64_t src_token_stride, int64_t src_layer_stride,
+                        const int64_t *slot_mapping, int64_t num_tokens, int src_dtype,
+                        uint64_t *k_digest, uint64_t *v_digest, void *stream);
+
 /* Slot resolution + reshape_and_cache that allocates nothing. No counterpart
  * in the reference.
  *

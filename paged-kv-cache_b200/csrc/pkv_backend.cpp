@@ -653,6 +653,47 @@ Status B200Backend::digest(uint64_t *k, uint64_t *v, cudaStream_t st) {
     return Status::Ok();
 }
 
+Status B200Backend::digest_rows(int64_t layer, const void *k, const void *v, int64_t tok_stride,
+                                int64_t layer_stride, const int64_t *slots, int64_t num_tokens,
+                                DType src, uint64_t *kd, uint64_t *vd, cudaStream_t st) {
+    if (layer < -1 || (layer >= 0 && (uint64_t)layer >= cfg_.num_layers))
+        return error(PKV_ERR_INVALID_LAYER, layer, (int64_t)cfg_.num_layers,
+                     msg_layer((uint64_t)layer, cfg_.num_layers));
+    if (num_tokens < 0) return error(PKV_ERR_SHAPE_MISMATCH, 0, num_tokens, "negative token count");
+    if (num_tokens > 0 && (!k || !v || !slots)) return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    if (tok_stride <= 0) tok_stride = (int64_t)shard_entry_;
+    const bool all = layer == -1;
+    if (all && layer_stride <= 0) layer_stride = tok_stride * num_tokens;
+    DeviceGuard g(device_);
+    unsigned long long host[2] = {0, 0};
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(d_digest_, 0, sizeof(host), st)) != cudaSuccess)
+        return device_error("digest_rows", e);
+    DigestRowsLaunch a{};
+    a.k = k;
+    a.v = v;
+    a.src_token_stride = tok_stride;
+    a.src_layer_stride = all ? layer_stride : 0;
+    a.slots = reinterpret_cast<const long long *>(slots);
+    a.num_tokens = num_tokens;
+    a.num_layers = all ? (long long)cfg_.num_layers : 1;
+    a.first_layer = all ? 0 : layer;
+    a.slots_per_layer = (long long)slots_per_layer();
+    a.entry_elems = (long long)shard_entry_;
+    a.full_entry = (long long)full_entry_elems();
+    a.elem_offset = (long long)elem_offset();
+    a.src_dtype = src;
+    a.pool_dtype = dtype_;
+    a.out = d_digest_;
+    if ((e = launch_digest_rows(a, sms_, st)) != cudaSuccess) return device_error("digest_rows", e);
+    if ((e = cudaMemcpyAsync(host, d_digest_, sizeof(host), cudaMemcpyDeviceToHost, st)) ||
+        (e = cudaStreamSynchronize(st)))
+        return device_error("digest_rows", e);
+    *kd = host[0];
+    *vd = host[1];
+    return Status::Ok();
+}
+
 Status B200Backend::sync() {
     DeviceGuard g(device_);
     return check("cudaStreamSynchronize", cudaStreamSynchronize(stream_));

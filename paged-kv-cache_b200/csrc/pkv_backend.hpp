@@ -65,6 +65,9 @@ class B200Backend {
                              const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
                              int32_t *cu, int64_t *slots, cudaStream_t s);
     Status digest(uint64_t *k, uint64_t *v, cudaStream_t s);
+    Status digest_rows(int64_t layer, const void *k, const void *v, int64_t tok_stride,
+                       int64_t layer_stride, const int64_t *slots, int64_t num_tokens, DType src,
+                       uint64_t *kd, uint64_t *vd, cudaStream_t s);
     Status sync();
     Status take_device_error(int64_t *index);
 

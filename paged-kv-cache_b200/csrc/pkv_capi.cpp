@@ -201,6 +201,19 @@ int pkv_digest(pkv_backend *b, uint64_t *k_digest, uint64_t *v_digest, void *str
     return guarded([&] { return b->impl->digest(k_digest, v_digest, as_stream(stream)); });
 }
 
+int pkv_digest_rows_dev(pkv_backend *b, int64_t layer, const void *k, const void *v,
+                        int64_t src_token_stride, int64_t src_layer_stride,
+                        const int64_t *slot_mapping, int64_t num_tokens, int src_dtype,
+                        uint64_t *k_digest, uint64_t *v_digest, void *stream) {
+    if (!b || !k_digest || !v_digest) return null_handle();
+    if (!valid_dtype(src_dtype)) return bad_dtype();
+    return guarded([&] {
+        return b->impl->digest_rows(layer, k, v, src_token_stride, src_layer_stride, slot_mapping,
+                                    num_tokens, static_cast<pkv::DType>(src_dtype), k_digest,
+                                    v_digest, as_stream(stream));
+    });
+}
+
 int pkv_sync(pkv_backend *b) {
     if (!b) return null_handle();
     return guarded([&] { return b->impl->sync(); });

@@ -88,6 +88,25 @@ struct DigestLaunch {
     unsigned long long *out;   // [2]: K digest, V digest (accumulated)
 };
 
+// Digest of rows as a scatter into an empty pool would store them.
+struct DigestRowsLaunch {
+    const void *k;
+    const void *v;
+    long long src_token_stride;  // elements
+    long long src_layer_stride;  // elements
+    const long long *slots;
+    long long num_tokens;
+    long long num_layers;
+    long long first_layer;
+    long long slots_per_layer;
+    long long entry_elems;
+    long long full_entry;
+    long long elem_offset;
+    DType src_dtype;
+    DType pool_dtype;
+    unsigned long long *out;  // [2], accumulated
+};
+
 int num_sms(int device);
 
 cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t s);
@@ -95,5 +114,6 @@ cudaError_t launch_copy_blocks(const CopyLaunch &a, cudaStream_t s);
 cudaError_t launch_zero_blocks(const ZeroLaunch &a, cudaStream_t s);
 cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t s);
+cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t s);
 
 }  // namespace pkv

@@ -386,6 +386,45 @@ digest_kernel(const T *__restrict__ kp, const T *__restrict__ vp, long long rows
     if ((threadIdx.x & 31) == 0 && acc) atomicAdd(out + plane, acc);
 }
 
+// Digest that a pool would have after `num_layers` layers of rows were
+// scattered through `slots` into it while it was empty: the same per-element
+// hash, over the value as the pool would store it.
+__device__ __forceinline__ unsigned widen_value(float x) { return __float_as_uint(x); }
+__device__ __forceinline__ unsigned widen_value(__nv_bfloat16 x) {
+    return (unsigned)(*reinterpret_cast<const unsigned short *>(&x)) << 16;
+}
+__device__ __forceinline__ unsigned widen_value(__half x) { return __float_as_uint(__half2float(x)); }
+
+template <typename S, typename D>
+__global__ void __launch_bounds__(kThreads)
+digest_rows_kernel(const S *__restrict__ k, const S *__restrict__ v, long long tok_stride,
+                   long long layer_stride, const long long *__restrict__ slots, long long num_tokens,
+                   long long entry, long long num_layers, long long first_layer,
+                   long long slots_per_layer, long long full_entry, long long elem_offset,
+                   unsigned long long *out) {
+    const int plane = blockIdx.y;
+    const S *src = plane ? v : k;
+    const long long total = num_layers * num_tokens * entry;
+    unsigned long long acc = 0;
+    const long long stride = (long long)gridDim.x * kThreads;
+    for (long long i = (long long)blockIdx.x * kThreads + threadIdx.x; i < total; i += stride) {
+        const long long r = i / entry;
+        const long long e = i - r * entry;
+        const long long l = r / num_tokens;
+        const long long t = r - l * num_tokens;
+        const long long s = __ldg(slots + t);
+        if (s < 0 || s >= slots_per_layer) continue;
+        const D d = from_f32<D>(to_f32(src[l * layer_stride + t * tok_stride + e]));
+        const unsigned bits = widen_value(d);
+        if (bits == 0) continue;
+        const long long gidx = ((first_layer + l) * slots_per_layer + s) * full_entry + elem_offset + e;
+        acc += mix64(((unsigned long long)gidx * 2 + plane) * 0x9E3779B97F4A7C15ull + bits);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0 && acc) atomicAdd(out + plane, acc);
+}
+
 // ---- helpers ---------------------------------------------------------------------
 
 inline bool aligned(const void *p, long long a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -589,6 +628,39 @@ cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t st) {
             break;
     }
     return cudaGetLastError();
+}
+
+namespace {
+template <typename S, typename D>
+cudaError_t digest_rows_sd(const DigestRowsLaunch &a, int sms, cudaStream_t st) {
+    const long long total = a.num_layers * a.num_tokens * a.entry_elems;
+    long long bx = std::min<long long>((total + kThreads - 1) / kThreads, (long long)sms * 16);
+    dim3 grid((unsigned)std::max<long long>(bx, 1), 2);
+    digest_rows_kernel<S, D><<<grid, kThreads, 0, st>>>(
+        static_cast<const S *>(a.k), static_cast<const S *>(a.v), a.src_token_stride,
+        a.src_layer_stride, a.slots, a.num_tokens, a.entry_elems, a.num_layers, a.first_layer,
+        a.slots_per_layer, a.full_entry, a.elem_offset, a.out);
+    return cudaGetLastError();
+}
+template <typename S>
+cudaError_t digest_rows_s(const DigestRowsLaunch &a, int sms, cudaStream_t st) {
+    switch (a.pool_dtype) {
+        case DType::F32: return digest_rows_sd<S, float>(a, sms, st);
+        case DType::BF16: return digest_rows_sd<S, __nv_bfloat16>(a, sms, st);
+        case DType::F16: return digest_rows_sd<S, __half>(a, sms, st);
+    }
+    return cudaErrorInvalidValue;
+}
+}  // namespace
+
+cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t st) {
+    if (a.num_layers * a.num_tokens * a.entry_elems <= 0) return cudaSuccess;
+    switch (a.src_dtype) {
+        case DType::F32: return digest_rows_s<float>(a, sms, st);
+        case DType::BF16: return digest_rows_s<__nv_bfloat16>(a, sms, st);
+        case DType::F16: return digest_rows_s<__half>(a, sms, st);
+    }
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace pkv

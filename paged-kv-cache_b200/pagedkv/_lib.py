@@ -65,6 +65,8 @@ _PROTOS = {
     "pkv_digest": (_I, [_P, C.POINTER(_U64), C.POINTER(_U64), _P]),
     "pkv_resolve_and_cache_noalloc": (_I, [C.POINTER(Config), _I, _I, _I, _P, _P, _P, _I64, _P, _P,
                                            _I64, _I64, _P, _I64, _P, _P, _I64, _I64, _I, _P, _P]),
+    "pkv_digest_rows_dev": (_I, [_P, _I64, _P, _P, _I64, _I64, _P, _I64, _I, C.POINTER(_U64),
+                                 C.POINTER(_U64), _P]),
     "pkv_sync": (_I, [_P]),
     "pkv_device_error": (_I, [_P, C.POINTER(_I64)]),
 }

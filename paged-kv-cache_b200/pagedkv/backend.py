@@ -227,6 +227,20 @@ class B200Backend:
         _check(lib.pkv_digest(self._h, C.byref(k), C.byref(v), _stream_ptr(stream)))
         return k.value, v.value
 
+    def digest_rows(self, k, v, slot_mapping, layer: int | None = None, stream=None) -> tuple[int, int]:
+        """Digests the pool would have if these rows were its only contents."""
+        tag = _torch_tag(k)
+        if layer is None:
+            n_tok, tok_stride, layer_stride, lay = k.shape[1], k.stride(1), k.stride(0), -1
+        else:
+            n_tok, tok_stride, layer_stride, lay = k.shape[0], k.stride(0), 0, layer
+        _same_layout(k, v)
+        kd, vd = C.c_uint64(), C.c_uint64()
+        _check(lib.pkv_digest_rows_dev(self._h, lay, _ptr(k), _ptr(v), tok_stride, layer_stride,
+                                       _ptr(slot_mapping), n_tok, tag, C.byref(kd), C.byref(vd),
+                                       _stream_ptr(stream)))
+        return kd.value, vd.value
+
     def sync(self) -> None:
         _check(lib.pkv_sync(self._h))
 

@@ -443,3 +443,33 @@ def test_head_shards_reassemble_to_the_oracle_pool(cuda, shards):
     kd = sum(b.digest()[0] for b in backs) % (1 << 64)
     vd = sum(b.digest()[1] for b in backs) % (1 << 64)
     assert (kd, vd) == cpu.digest()
+
+
+@pytest.mark.parametrize("src", ["bf16", "f32"])
+def test_rows_digest_predicts_the_pool_digest(cuda, src):
+    """pkv_digest_rows_dev (used to verify shards without reading pools back)
+    equals pkv_digest of the pool the rows were written into."""
+    import torch
+
+    cfg = CacheConfig(64, 16, 4, 32, 3, 2)
+    e = cfg.entry_elems()
+    st = Stream(31)
+    slots = torch.from_numpy(st.permutation(cfg.num_blocks * cfg.block_size)[:500].astype(np.int64)).to(cuda)
+    slots[9] = -1
+    dt = torch.bfloat16 if src == "bf16" else torch.float32
+    k = torch.randn((cfg.num_layers, 500, e), device=cuda).to(dt)
+    v = torch.randn((cfg.num_layers, 500, e), device=cuda).to(dt)
+    for shards in (1, 2):
+        digs, rows = [], []
+        for r in range(shards):
+            w = e // shards
+            b = B200Backend(cfg, dtype="bf16", shard_rank=r, num_shards=shards)
+            ks, vs = k[..., r * w:(r + 1) * w], v[..., r * w:(r + 1) * w]
+            b.reshape_and_cache(ks, vs, slots)
+            digs.append(b.digest())
+            rows.append(b.digest_rows(ks, vs, slots))
+            assert digs[-1] == rows[-1]
+        if shards == 1:
+            whole = digs[0]
+        else:
+            assert tuple(sum(d[i] for d in digs) % 2**64 for i in range(2)) == whole

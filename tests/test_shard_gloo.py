@@ -1,0 +1,86 @@
+"""The N>1 path on CPU: two gloo ranks, each holding one KV-head shard of a
+pool (written through the oracle), verify the shards with the same
+all-gather of digests that the benchmark runs over NCCL; a planted mistake
+in one rank's shard is caught."""
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _rank_main(rank: int, world: int, port: int, plant: bool, out_dir: str) -> None:
+    sys.path[:0] = [str(ROOT / "paged-kv-cache_b200"), str(ROOT)]
+    import torch.distributed as dist
+
+    from oracle.cpu import OracleBackend, digest_rows
+    from pagedkv.config import CacheConfig
+    from pagedkv.shard import entry_slice, verify_over_group
+    from pagedkv.workloads import Stream
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = CacheConfig(num_blocks=16, block_size=4, num_kv_heads=4, head_dim=8, num_layers=2,
+                      dtype_bytes=4)
+    e = cfg.entry_elems()
+    off, w = entry_slice(e, rank, world)
+    st = Stream(77)  # same inputs on every rank; each keeps its own columns
+    t = 20
+    slots = st.permutation(cfg.num_blocks * cfg.block_size)[:t]
+    dsts = [(int(s) // 4, int(s) % 4) for s in slots]
+    orc = OracleBackend(cfg)  # this rank's shard, held as a full-width pool zero outside the slice
+    pool, expect = [0, 0], [0, 0]
+    full_expect = [0, 0]
+    for layer in range(cfg.num_layers):
+        k = st.normal(t * e).astype(np.float32).reshape(t, e)
+        v = st.normal(t * e).astype(np.float32).reshape(t, e)
+        km, vm = np.zeros_like(k), np.zeros_like(v)
+        km[:, off:off + w], vm[:, off:off + w] = k[:, off:off + w], v[:, off:off + w]
+        if plant and rank == 1 and layer == 1:
+            km[3, off] += 1.0  # a wrong value lands in this shard only
+        orc.write_kv_batch(layer, dsts, km.ravel(), vm.ravel())
+        for p, rows in ((0, k), (1, v)):
+            masked = np.zeros_like(rows)
+            masked[:, off:off + w] = rows[:, off:off + w]
+            expect[p] += digest_rows(masked, slots, layer, cfg.num_blocks * cfg.block_size, p)
+            full_expect[p] += digest_rows(rows, slots, layer, cfg.num_blocks * cfg.block_size, p)
+    pool = orc.digest()
+    res = verify_over_group(tuple(pool), tuple(x % 2**64 for x in expect))
+    ok_total = int(res["pool_digest_k"], 16) == full_expect[0] % 2**64
+    Path(out_dir, f"rank{rank}.txt").write_text(f"{res['ok']} {res['shards_ok']} {ok_total}\n")
+    dist.destroy_process_group()
+
+
+def _run(plant: bool, tmp_path, port: int):
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_rank_main, args=(2, port, plant, str(tmp_path)), nprocs=2,
+                       start_method="spawn", join=True)
+    return [Path(tmp_path, f"rank{r}.txt").read_text().split(" ", 1) for r in range(2)]
+
+
+def test_two_gloo_ranks_verify_their_shards(tmp_path):
+    out = _run(False, tmp_path, 29531)
+    for ok, rest in out:
+        assert ok == "True" and rest.strip() == "[True, True] True"
+
+
+def test_a_wrong_value_in_one_shard_is_caught(tmp_path):
+    out = _run(True, tmp_path, 29532)
+    for ok, rest in out:
+        assert ok == "False" and rest.strip().startswith("[True, False]")
+
+
+def test_entry_slices_tile_the_entry():
+    sys.path[:0] = [str(ROOT / "paged-kv-cache_b200")]
+    from pagedkv.shard import entry_slice
+
+    for world in (1, 2, 4, 8):
+        cols = [c for r in range(world) for c in range(*(lambda o, w: (o, o + w))(*entry_slice(512, r, world)))]
+        assert cols == list(range(512))
+    with pytest.raises(ValueError):
+        entry_slice(512, 0, 3)
