@@ -297,7 +297,9 @@ def run_ours(args):
     if not verify["ok"]:
         raise SystemExit(f"bench: shard verification failed: {verify}")
 
-    tokens_all = T * world
+    # Every rank writes its head slice of all T tokens, so a step stores T
+    # whole tokens across the N GPUs.
+    tokens_all = T
     value = tokens_all * K / (total_ms / 1e3)
     eb = es * 2
     alg_bytes = T * L * 2 * eb * 2 + T * 8  # read + write K and V, one slot read per token
@@ -397,7 +399,7 @@ def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks
         one()
     barrier()
     dt = max_over_ranks(time.perf_counter() - t0)
-    return {"value": T * world * steps / dt, "unit": "tokens/s",
+    return {"value": T * steps / dt, "unit": "tokens/s",
             "h2d_bytes_per_step": int(L * (2 * T * es * 2 + T * 8)),
             "d2h_bytes_per_step": 16, "steps": steps,
             "path": "pkv_write_kv_batch per layer, pinned bf16 host rows, + pkv_device_error"}
