@@ -33,6 +33,8 @@ uint64_t pkv_allocator_num_free(const pkv_allocator *a);                    /* :
 uint64_t pkv_allocator_total_allocated(const pkv_allocator *a);             /* :85-87 */
 /* check_invariants (:213-240): PKV_OK, or PKV_ERR_DEVICE with the reason in pkv_last_error(). */
 int pkv_allocator_check_invariants(const pkv_allocator *a);
+/* Reference counts of n blocks at once (0 for free blocks); InvalidBlock on an id out of range. */
+int pkv_allocator_ref_counts(const pkv_allocator *a, const uint32_t *ids, uint64_t n, uint32_t *out);
 
 /* ---- BlockTable (crates/paged-kv-core/src/block_table.rs:20-240) ---- */
 pkv_table *pkv_table_new(uint64_t block_size);                              /* :46-52 */
@@ -74,6 +76,14 @@ typedef struct pkv_step_outcome {
     uint64_t num_finished;
     const uint32_t *freed_blocks; /* blocks whose refcount reached 0 this step (not in the reference's outcome) */
     uint64_t num_freed;
+    /* Per admitted sequence (in admitted order): the context length it was
+     * admitted with and its block table right after admission, as
+     * admitted_blocks[admitted_table_offsets[i] .. admitted_table_offsets[i+1]).
+     * The reference's admit discards append_many's slots (scheduler.rs:235-236);
+     * these tables are what device slot resolution rebuilds them from. */
+    const uint64_t *admitted_ctx;
+    const uint64_t *admitted_table_offsets; /* num_admitted + 1 entries */
+    const uint32_t *admitted_blocks;
 } pkv_step_outcome;
 
 pkv_scheduler *pkv_scheduler_new(uint64_t num_blocks, uint64_t block_size, uint64_t max_batch_size); /* :128-136 */

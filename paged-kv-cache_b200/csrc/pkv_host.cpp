@@ -230,7 +230,8 @@ struct Scheduler {
     std::vector<Running> running;
     // Last outcome.
     std::vector<uint64_t> admitted, preempted, finished, dec_id, dec_slot;
-    std::vector<uint32_t> dec_block, dec_src, dec_dst, freed_raw, freed;
+    std::vector<uint32_t> dec_block, dec_src, dec_dst, freed_raw, freed, adm_blocks;
+    std::vector<uint64_t> adm_ctx, adm_off;
     std::vector<int32_t> dec_cow;
 
     Scheduler(uint64_t nb, uint64_t bs, uint64_t mb) : alloc(nb), block_size(bs), max_batch(mb) {}
@@ -252,6 +253,9 @@ struct Scheduler {
             if (!s.ok()) return s;
             waiting.pop_front();
             admitted.push_back(p.id);
+            adm_ctx.push_back(p.context_len);
+            adm_blocks.insert(adm_blocks.end(), t.blocks.begin(), t.blocks.end());
+            adm_off.push_back(adm_blocks.size());
             running.push_back({p.id, std::move(t), p.max_new_tokens, 0});
         }
         return Status::Ok();
@@ -349,6 +353,9 @@ struct Scheduler {
         dec_dst.clear();
         freed_raw.clear();
         freed.clear();
+        adm_ctx.clear();
+        adm_blocks.clear();
+        adm_off.assign(1, 0);
         alloc.freed_log = &freed_raw;
         Status s = admit();
         if (s.ok()) s = decode();
@@ -377,6 +384,9 @@ struct Scheduler {
             out->num_finished = finished.size();
             out->freed_blocks = freed.data();
             out->num_freed = freed.size();
+            out->admitted_ctx = adm_ctx.data();
+            out->admitted_table_offsets = adm_off.data();
+            out->admitted_blocks = adm_blocks.data();
         }
         return s;
     }
@@ -431,6 +441,14 @@ int pkv_allocator_ref_count(const pkv_allocator *a, uint32_t id, uint32_t *count
 uint64_t pkv_allocator_num_free(const pkv_allocator *a) { return a->a.free_list.size(); }
 uint64_t pkv_allocator_total_allocated(const pkv_allocator *a) { return a->a.total_allocated; }
 int pkv_allocator_check_invariants(const pkv_allocator *a) { return finish(a->a.check_invariants()); }
+int pkv_allocator_ref_counts(const pkv_allocator *a, const uint32_t *ids, uint64_t n, uint32_t *out) {
+    for (uint64_t i = 0; i < n; ++i) {
+        pkv::Status s = a->a.validate(ids[i]);
+        if (!s.ok()) return finish(s);
+        out[i] = a->a.rc[ids[i]];
+    }
+    return finish(pkv::Status::Ok());
+}
 
 pkv_table *pkv_table_new(uint64_t block_size) {
     if (block_size == 0) return nullptr;

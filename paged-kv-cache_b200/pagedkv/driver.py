@@ -1,0 +1,144 @@
+"""The StepOutcome driver: applies StepPlans (pagedkv.traces) to a B200Backend.
+
+One step issues, on one CUDA stream and in the order the scheduler's
+contract requires (crates/paged-kv-core/src/scheduler.rs:57-63):
+
+1. copy_blocks of the step's copy-on-write pairs,
+2. slot resolution for the sequences given as block tables,
+3. one all-layer reshape_and_cache for every new token,
+4. zero_blocks of the blocks freed this step.
+
+Step metadata travels host -> device through reused pinned buffers; nothing
+is allocated per step once the buffers have grown to the largest step.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .backend import B200Backend
+from .traces import StepPlan
+
+
+class _Staging:
+    """A pinned host buffer and a device buffer of int64 words, grown on demand."""
+
+    def __init__(self, dev):
+        import torch
+
+        self.torch = torch
+        self.dev = dev
+        self.host = torch.empty(0, dtype=torch.int64).pin_memory()
+        self.device = torch.empty(0, dtype=torch.int64, device=dev)
+        self.event = None
+
+    def upload(self, arrays: list[np.ndarray], stream):
+        """Copy the int arrays (as int64 words, each 8-byte aligned) to the device
+        on `stream`; returns a device int64 view per array."""
+        torch = self.torch
+        words = [(a.nbytes + 7) // 8 for a in arrays]
+        total = max(sum(words), 1)
+        if self.event is not None:
+            self.event.synchronize()  # the previous step's copy out of `host` is done
+        if self.host.numel() < total:
+            self.host = torch.empty(2 * total, dtype=torch.int64).pin_memory()
+        if self.device.numel() < total:
+            self.device = torch.empty(2 * total, dtype=torch.int64, device=self.dev)
+        hb = self.host.numpy().view(np.uint8)
+        off = 0
+        for a, w in zip(arrays, words):
+            hb[off * 8: off * 8 + a.nbytes] = np.ascontiguousarray(a).view(np.uint8).ravel()
+            off += w
+        with torch.cuda.stream(stream):
+            self.device[:total].copy_(self.host[:total], non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record(stream)
+        out, off = [], 0
+        for w in words:
+            out.append(self.device[off: off + w])
+            off += w
+        return out
+
+
+class DeviceStepper:
+    def __init__(self, backend: B200Backend, stream=None):
+        import torch
+
+        self.torch = torch
+        self.b = backend
+        self.dev = torch.device("cuda", backend.device)
+        self.stream = stream or torch.cuda.current_stream(self.dev)
+        self.stage = _Staging(self.dev)
+        self.slots = torch.empty(0, dtype=torch.int64, device=self.dev)
+        self.cu = torch.empty(0, dtype=torch.int32, device=self.dev)
+        self.launches = 0
+
+    def _ensure(self, t: int, s: int):
+        torch = self.torch
+        if self.slots.numel() < t:
+            self.slots = torch.empty(max(2 * t, 1024), dtype=torch.int64, device=self.dev)
+        if self.cu.numel() < s + 1:
+            self.cu = torch.empty(max(2 * (s + 1), 1024), dtype=torch.int32, device=self.dev)
+
+    def apply(self, plan: StepPlan, k, v) -> int:
+        """Runs one step. k, v: device [L][R][entry] rows; token i of the step
+        reads row i % R (R >= the step's token count keeps every row distinct)."""
+        torch = self.torch
+        b, st = self.b, self.stream
+        tr, d = plan.resolved_tokens, len(plan.direct_slots)
+        t, s = tr + d, len(plan.new)
+        self._ensure(t, s)
+        tables = np.ascontiguousarray(plan.tables, np.int32)
+        copies, ctx, new, direct, zero = (np.ascontiguousarray(plan.copies, np.int64),
+                                          np.ascontiguousarray(plan.ctx, np.int32),
+                                          np.ascontiguousarray(plan.new, np.int32),
+                                          np.ascontiguousarray(plan.direct_slots, np.int64),
+                                          np.ascontiguousarray(plan.zero, np.int64))
+        d_copies, d_tables, d_ctx, d_new, d_direct, d_zero = self.stage.upload(
+            [copies, tables, ctx, new, direct, zero], st)
+        n = 0
+        if len(copies):
+            b.copy_blocks_dev(d_copies, count=len(copies), stream=st)
+            n += 1
+        if s:
+            b.resolve_slots(d_tables.view(torch.int32)[: tables.size].view(tables.shape),
+                            d_ctx.view(torch.int32)[:s], d_new.view(torch.int32)[:s], tr,
+                            self.cu, self.slots[:max(tr, 1)], stream=st)
+            n += 1
+        if d:
+            with torch.cuda.stream(st):
+                self.slots[tr:t].copy_(d_direct[:d], non_blocking=True)
+        rows = k.shape[1]
+        for c0 in range(0, t, rows):
+            c = min(rows, t - c0)
+            b.reshape_and_cache(k[:, :c], v[:, :c], self.slots[c0:c0 + c], stream=st)
+            n += 1
+        if len(zero):
+            b.zero_blocks_dev(d_zero, count=len(zero), stream=st)
+            n += 1
+        self.launches += n
+        return n
+
+
+def apply_to_oracle(orc, plan: StepPlan, k: np.ndarray, v: np.ndarray, resolve) -> None:
+    """The same step on the CPU oracle (CpuBackend semantics): copies, writes
+    of every token (slots resolved by the oracle's slot rule), zeroes.
+    k, v: f32 [L][R][entry]; token i uses row i % R."""
+    cfg = orc.cfg
+    bs = cfg.block_size
+    if len(plan.copies):
+        orc.copy_blocks(plan.copies)
+    tr = plan.resolved_tokens
+    if len(plan.new):
+        rc, _, res = resolve(plan.tables, plan.ctx, plan.new, tr, bs, cfg.num_blocks)
+        assert rc == 0
+    else:
+        res = np.zeros(0, np.int64)
+    slots = np.concatenate([res, plan.direct_slots.astype(np.int64)])
+    rows = np.arange(len(slots)) % k.shape[1]
+    keep = slots >= 0
+    dsts = [(int(x) // bs, int(x) % bs) for x in slots[keep]]
+    for layer in range(cfg.num_layers):
+        orc.write_kv_batch(layer, dsts, k[layer][rows[keep]].ravel(), v[layer][rows[keep]].ravel())
+    if len(plan.zero):
+        orc.zero_blocks(plan.zero)

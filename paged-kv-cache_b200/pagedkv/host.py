@@ -29,6 +29,8 @@ class _Outcome(C.Structure):
         ("preempted", C.POINTER(_U64)), ("num_preempted", _U64),
         ("finished", C.POINTER(_U64)), ("num_finished", _U64),
         ("freed_blocks", C.POINTER(_U32)), ("num_freed", _U64),
+        ("admitted_ctx", C.POINTER(_U64)), ("admitted_table_offsets", C.POINTER(_U64)),
+        ("admitted_blocks", C.POINTER(_U32)),
     ]
 
 
@@ -41,6 +43,7 @@ for _n, _r, _a in [
     ("pkv_allocator_ref_count", _I, [_P, _U32, C.POINTER(_U32)]),
     ("pkv_allocator_num_free", _U64, [_P]), ("pkv_allocator_total_allocated", _U64, [_P]),
     ("pkv_allocator_check_invariants", _I, [_P]),
+    ("pkv_allocator_ref_counts", _I, [_P, _P, _U64, _P]),
     ("pkv_table_new", _P, [_U64]), ("pkv_table_free_handle", None, [_P]),
     ("pkv_table_num_tokens", _U64, [_P]), ("pkv_table_num_blocks", _U64, [_P]),
     ("pkv_table_blocks", _U64, [_P, _P, _U64]),
@@ -117,6 +120,12 @@ class BlockAllocator:
 
     def check_invariants(self) -> None:
         _check(lib.pkv_allocator_check_invariants(self._h))
+
+    def ref_counts(self, ids: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        out = np.zeros(max(ids.size, 1), np.uint32)
+        _check(lib.pkv_allocator_ref_counts(self._h, ids.ctypes.data, ids.size, out.ctypes.data))
+        return out[: ids.size]
 
 
 class BlockTable:
@@ -215,7 +224,12 @@ class Scheduler:
         o = _Outcome()
         _check(lib.pkv_scheduler_step(self._h, C.byref(o)))
         nd = o.num_decoded
+        na = o.num_admitted
+        off = _arr(o.admitted_table_offsets, na + 1, np.int64)
         return {
+            "admitted_ctx": _arr(o.admitted_ctx, na, np.int64),
+            "admitted_table_offsets": off,
+            "admitted_blocks": _arr(o.admitted_blocks, int(off[-1]) if na else 0, np.int64),
             "admitted": _arr(o.admitted, o.num_admitted, np.uint64),
             "decoded_id": _arr(o.decoded_id, nd, np.uint64),
             "decoded_block": _arr(o.decoded_block, nd, np.int64),
