@@ -47,6 +47,13 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["prefill", "decode", "cow", "churn"], default="prefill",
+                   help="prefill: ragged 65,536-token chunk (headline); decode: 256-sequence "
+                        "decode step; cow: beam-search copy-on-write trace; churn: "
+                        "continuous-batching trace at 70B-like geometry")
+    p.add_argument("--fork-rate", type=float, default=0.05,
+                   help="churn: probability per step of forking a running sequence")
+    p.add_argument("--no-graph", action="store_true", help="decode: launch instead of graph replay")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-ops", action="store_true")
@@ -185,46 +192,136 @@ def host_slots(tables, ctx, new, block_size):
 # ---- our arm ----------------------------------------------------------------------------------
 
 
-def run_ours(args):
-    import numpy as np
-    import torch
-    import torch.distributed as dist
+class Run:
+    """One rank of the benchmark: device, stream, process group and timing helpers."""
 
-    from pagedkv import B200Backend, CacheConfig
+    def __init__(self, args):
+        import torch
+        import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.gpus != world and world > 1:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
+        self.args = args
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if args.gpus != self.world and self.world > 1:
+            raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {self.world}")
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=self.dev)
+        self.stream = torch.cuda.Stream(device=self.dev)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
+    def max_over_ranks(self, x: float) -> float:
+        if self.world == 1:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
-    cfg, tables, ctx, new = build_batch(world, args.chunk_tokens, args.chunk_prompts,
-                                        args.chunk_blocks)
-    T = int(new.sum())
-    S = len(new)
-    backend = B200Backend(cfg, dtype="bf16", device=local, shard_rank=rank, num_shards=world)
-    es = backend.shard_entry_elems
-    L = cfg.num_layers
+    def load(self, step, seconds: float) -> None:
+        """Untimed steps that keep the GPU busy while the clocks are sampled."""
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            with self.torch.cuda.stream(self.stream):
+                for _ in range(20):
+                    step()
+            self.stream.synchronize()
 
-    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    def timed_steps(self, step, K: int, marks_per_step: int = 1):
+        """K steps between CUDA events on the benchmark stream, with the
+        clocks sampled over 1.3 s of continuous load around them. `step(i, ev)`
+        records its own inner events into ev (a list) if it wants."""
+        torch = self.torch
+        evs = []
+        self.barrier()
+        with ClockSampler(self.local) as clocks:
+            self.load(lambda: step(-1, None), 1.0)
+            self.barrier()
+            start = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(self.stream):
+                start.record(self.stream)
+                for i in range(K):
+                    ev = []
+                    step(i, ev)
+                    evs.append(ev)
+                end = torch.cuda.Event(enable_timing=True)
+                end.record(self.stream)
+            self.barrier()
+            self.load(lambda: step(-1, None), 0.3)
+        self.barrier()
+        total = self.max_over_ranks(start.elapsed_time(end))
+        return total, evs, {**clocks.summary(),
+                            "window": "sampled every 200 ms over 1.3 s of continuous load "
+                                      "around the timed steps"}
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def _event_ms(evs, i, j):
+    return sum(e[i].elapsed_time(e[j]) for e in evs) / max(len(evs), 1)
+
+
+def base_line(run, value, K, ms_per_step, scaling, workload, extra_config, data) -> dict:
+    return {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": run.world, "steps": K,
+        "warmup": run.args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": data,
+        "config": {"workload": workload, **extra_config},
+    }
+
+
+def roofline(kernel, alg_bytes, kernel_ms, traffic=None) -> dict:
+    peak, peak_kind = measured_peak_gbs()
+    achieved = alg_bytes / (kernel_ms / 1e3) / 1e9
+    return {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak,
+            "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+            "algorithmic_bytes_per_launch": alg_bytes, "kernel_ms": kernel_ms}
+
+
+def check_rows_landed(backend, k, v, d_slots, T, L):
+    """Every token's entry is in its slot (strided sample of tokens, 3 layers)."""
+    torch = __import__("torch")
+    es = k.shape[2]
+    pk, pv = backend.planes()
+    stride = max(1, T // 4096)
+    idx = torch.arange(0, T, stride, device=k.device)
+    chk = d_slots[idx]
+    ok = all(torch.equal(pk[l].reshape(-1, es)[chk], k[l, idx]) and
+             torch.equal(pv[l].reshape(-1, es)[chk], v[l, idx]) for l in (0, L // 2, L - 1))
+    if not ok:
+        raise SystemExit("bench: pool contents differ from the inputs")
+
+
+def wl_table_batch(run, kind: str) -> dict:
+    """Prefill chunk (config 3, the headline) or decode step (config 2): one
+    step = device slot resolution + one all-layer reshape_and_cache."""
+    import numpy as np
+
+    torch = run.torch
+    from pagedkv import B200Backend
+    from pagedkv.shard import verify_over_group
+
+    args, world, dev, stream = run.args, run.world, run.dev, run.stream
+    if kind == "prefill":
+        cfg, tables, ctx, new = build_batch(world, args.chunk_tokens, args.chunk_prompts,
+                                            args.chunk_blocks)
+    else:
+        cfg, tables, ctx, new = build_decode(world)
+    T, S = int(new.sum()), len(new)
+    backend = B200Backend(cfg, dtype="bf16", device=run.local, shard_rank=run.rank, num_shards=world)
+    es, L = backend.shard_entry_elems, cfg.num_layers
+    gen = torch.Generator(device=dev).manual_seed(1000 + run.rank)
     k = torch.randn((L, T, es), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     v = torch.randn((L, T, es), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     d_tab = torch.from_numpy(tables).to(dev)
@@ -232,65 +329,64 @@ def run_ours(args):
     d_new = torch.from_numpy(new).to(dev)
     d_cu = torch.empty(S + 1, dtype=torch.int32, device=dev)
     d_slots = torch.empty(T, dtype=torch.int64, device=dev)
-    stream = torch.cuda.Stream(device=dev)
 
-    def step():
+    def launch():
         backend.resolve_slots(d_tab, d_ctx, d_new, T, d_cu, d_slots, stream=stream)
         backend.reshape_and_cache(k, v, d_slots, stream=stream)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            step()
-    barrier()
+            launch()
+    run.barrier()
     if backend.device_error() is not None:
         raise SystemExit(f"device error in warm-up: {backend.device_error()}")
+    check_rows_landed(backend, k, v, d_slots, T, L)
 
-    # Correctness of the timed configuration: every token's entry landed in its slot.
-    pk, pv = backend.planes()
-    slot_host = d_slots.cpu().numpy()
-    chk = torch.from_numpy(slot_host[:: max(1, T // 4096)]).to(dev)
-    idx = torch.arange(0, T, max(1, T // 4096), device=dev)
-    ok = all(torch.equal(pk[l].reshape(-1, es)[chk], k[l, idx]) and
-             torch.equal(pv[l].reshape(-1, es)[chk], v[l, idx]) for l in (0, L // 2, L - 1))
-    if not ok:
-        raise SystemExit("bench: pool contents differ from the inputs")
+    graph = None
+    if kind == "decode" and not args.no_graph:
+        # The decode step is launch-bound: replay it as one CUDA graph.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            launch()
+        torch.cuda.synchronize()
+
+    def step(i, ev):
+        if graph is not None:
+            graph.replay()
+            return
+        if ev is not None:
+            for _ in range(3):
+                ev.append(torch.cuda.Event(enable_timing=True))
+            ev[0].record(stream)
+            backend.resolve_slots(d_tab, d_ctx, d_new, T, d_cu, d_slots, stream=stream)
+            ev[1].record(stream)
+            backend.reshape_and_cache(k, v, d_slots, stream=stream)
+            ev[2].record(stream)
+        else:
+            launch()
 
     K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-
-    def load(seconds: float) -> None:
-        """Untimed steps that keep the GPU busy while the clocks are sampled."""
-        t0 = time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            with torch.cuda.stream(stream):
-                for _ in range(20):
-                    step()
-            stream.synchronize()
-
-    barrier()
-    with ClockSampler(local) as clocks:
-        load(1.0)
-        barrier()
+    total_ms, evs, clocks = run.timed_steps(step, K)
+    eb = es * 2
+    alg_bytes = T * L * 2 * eb * 2 + T * 8  # read + write K and V, one slot read per token
+    if graph is None:
+        reshape_ms = run.max_over_ranks(_event_ms(evs, 1, 2))
+        resolve_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
+    else:
+        # Kernel time of the graph's reshape: the same launch timed on its own.
+        evs2 = []
         with torch.cuda.stream(stream):
-            for i in range(K):
-                ev[i][0].record(stream)
+            for _ in range(max(K, 10)):
+                e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                e[0].record(stream)
                 backend.resolve_slots(d_tab, d_ctx, d_new, T, d_cu, d_slots, stream=stream)
-                ev[i][1].record(stream)
+                e[1].record(stream)
                 backend.reshape_and_cache(k, v, d_slots, stream=stream)
-                ev[i][2].record(stream)
-        barrier()
-        load(0.3)
-    barrier()
-    total_ms = ev[0][0].elapsed_time(ev[K - 1][2])
-    resolve_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(K)]
-    reshape_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(K)]
-    total_ms = max_over_ranks(total_ms)
-    reshape_avg = max_over_ranks(sum(reshape_ms) / K)
-    resolve_avg = max_over_ranks(sum(resolve_ms) / K)
-
-    # Shard verification: each rank digests its shard and the rows it wrote;
-    # the ranks all-gather the digests (NCCL) and check them.
-    from pagedkv.shard import verify_over_group
+                e[2].record(stream)
+                evs2.append(e)
+        stream.synchronize()
+        reshape_ms = run.max_over_ranks(_event_ms(evs2, 1, 2))
+        resolve_ms = run.max_over_ranks(_event_ms(evs2, 0, 1))
 
     verify = verify_over_group(backend.digest(stream=stream),
                                backend.digest_rows(k, v, d_slots, stream=stream), device=dev)
@@ -299,81 +395,177 @@ def run_ours(args):
 
     # Every rank writes its head slice of all T tokens, so a step stores T
     # whole tokens across the N GPUs.
-    tokens_all = T
-    value = tokens_all * K / (total_ms / 1e3)
-    eb = es * 2
-    alg_bytes = T * L * 2 * eb * 2 + T * 8  # read + write K and V, one slot read per token
-    peak, peak_kind = measured_peak_gbs()
-    achieved = alg_bytes / (reshape_avg / 1e3) / 1e9
-
-    out = {
-        "metric": METRIC,
-        "value": value,
-        "unit": "tokens/s",
-        "n_gpus": world,
-        "steps": K,
-        "warmup": args.warmup,
-        "ms_per_step": total_ms / K,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (seeded: log-uniform prompt lengths, shuffled free list, normal K/V)",
-        "config": {
-            "workload": f"ragged prefill chunk x{world}: {world}x{args.chunk_tokens} tokens "
-                        f"({S} prompts, log-uniform 128..4096), Qwen2-7B KV geometry "
-                        f"(28 layers, 4 KV heads x 128, bs 16), pool {cfg.num_blocks} blocks "
-                        f"head-sharded {world} ways; step = device slot resolution + "
-                        "all-layer reshape_and_cache",
-            "tokens_per_step": tokens_all,
-            "layers": L,
-            "entry_elems_per_gpu": es,
-            "pool_gib_per_gpu": round(backend.allocated_bytes() / 2**30, 2),
-            "parallelism": f"kv-head shards x{world}",
-            "l2": "inputs (K/V %.2f GiB per GPU) exceed the 126 MB L2; no flush needed" %
-                  (2 * L * T * eb / 2**30),
-        },
-        "gb_per_s": alg_bytes * world / (total_ms / K / 1e3) / 1e9,
-        "roofline": {
-            "kernel": "reshape_copy_kernel (all layers)",
-            "bound": "hbm",
-            "achieved": achieved,
-            "peak": peak,
-            "peak_kind": peak_kind,
-            "unit": "GB/s",
-            "frac": achieved / peak,
-            "traffic": profile_traffic("reshape_prefill_ncu"),
-            "algorithmic_bytes_per_launch": alg_bytes,
-            "kernel_ms": reshape_avg,
-        },
-        "resolve_slots_ms": resolve_avg,
-        "gpu_launches": 2 * K,
-        "verify": verify,
-        "clocks": {**clocks.summary(),
-                   "window": "sampled every 200 ms over 1.3 s of continuous load around the timed steps"},
-    }
-
-    if not args.no_ops and rank == 0:
+    if kind == "prefill":
+        workload = (f"ragged prefill chunk x{world}: {world}x{args.chunk_tokens} tokens ({S} prompts, "
+                    "log-uniform 128..4096)")
+    else:
+        workload = f"decode step x{world}: {world}x256 sequences, context U[1,4096], +1 token each"
+    workload += (f", Qwen2-7B KV geometry (28 layers, 4 KV heads x 128, bs 16), pool "
+                 f"{cfg.num_blocks} blocks (shuffled free list) head-sharded {world} ways; step = "
+                 "device slot resolution + all-layer reshape_and_cache"
+                 + (" replayed as one CUDA graph" if graph is not None else ""))
+    out = base_line(run, T * K / (total_ms / 1e3), K, total_ms / K, "weak", workload, {
+        "tokens_per_step": T, "sequences_per_step": S, "layers": L, "entry_elems_per_gpu": es,
+        "pool_gib_per_gpu": round(backend.allocated_bytes() / 2**30, 2),
+        "parallelism": f"kv-head shards x{world}",
+        "l2": ("inputs (K/V %.2f GiB per GPU) exceed the 126 MB L2; no flush needed"
+               % (2 * L * T * eb / 2**30)) if 2 * L * T * eb > 2**28 else
+              "inputs (%.1f MiB) fit in L2; every step rewrites the same rows, as a decode "
+              "step re-reads a projection's fresh output" % (2 * L * T * eb / 2**20),
+    }, "synthetic (seeded: shuffled free list, " + ("log-uniform prompt lengths" if kind == "prefill"
+                                                       else "uniform context lengths") + ", normal K/V)")
+    out["gb_per_s"] = alg_bytes * world / (total_ms / K / 1e3) / 1e9
+    out["roofline"] = roofline("reshape_copy_kernel (all layers)", alg_bytes, reshape_ms,
+                               profile_traffic("reshape_prefill_ncu") if kind == "prefill" else None)
+    out["resolve_slots_ms"] = resolve_ms
+    out["gpu_launches"] = 2 * K
+    out["verify"] = verify
+    out["clocks"] = clocks
+    if kind == "prefill" and not args.no_ops and run.rank == 0:
         out["ops"] = bench_ops(backend, cfg, dev, stream)
-
     if not args.no_e2e:
-        out["e2e"] = e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks,
-                                   world)
-
-    if rank == 0 and world == 1 and not args.no_cpu:
-        n = 4096
+        out["e2e"] = e2e_host_path(args, backend, tables, ctx, new, k, v, run.barrier,
+                                   run.max_over_ranks)
+    if run.rank == 0 and world == 1 and not args.no_cpu:
+        n = min(4096, T)
         out["cpu_baseline"] = cpu_sample(tables, ctx, new, k[:, :n].float().cpu().numpy(),
                                          v[:, :n].float().cpu().numpy(), seconds=8.0, threads=1)
-
+    if graph is not None:
+        del graph
     backend.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(out), flush=True)
+    return out
 
 
-def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks, world):
+def build_decode(world: int):
+    """N decode batches of 256 sequences (config 2), batch c on its own
+    32,768-block range of the pool, each from a shuffled free list; batch c
+    uses the c-th seed (from 0 up) whose demand fits the range."""
+    import numpy as np
+
+    from pagedkv import CacheConfig
+    from pagedkv.workloads import decode_batch
+
+    cfg = CacheConfig(num_blocks=BLOCKS_PER_CHUNK * world, **GEOM)
+    one = CacheConfig(num_blocks=BLOCKS_PER_CHUNK, **GEOM)
+    parts, seed = [], 0
+    for c in range(world):
+        b = decode_batch(seed=None, first_seed=seed, cfg=one)
+        seed = b.seed + 1
+        t = b.tables.astype(np.int64)
+        t[t >= 0] += c * BLOCKS_PER_CHUNK
+        parts.append((b.ctx, b.new, t.astype(np.int32)))
+    return (cfg, np.concatenate([p[2] for p in parts]),
+            np.concatenate([p[0] for p in parts]).astype(np.int32),
+            np.concatenate([p[1] for p in parts]).astype(np.int32))
+
+
+def wl_trace(run, kind: str) -> dict:
+    """Config 4 (beam-search copy-on-write, Qwen2-7B geometry) or config 5
+    (continuous-batching churn, 70B-like geometry): a host trace of StepPlans
+    applied to the device by the StepOutcome driver, copy_blocks ->
+    resolve_slots -> reshape_and_cache -> zero_blocks per step."""
+    import numpy as np
+
+    torch = run.torch
+    from pagedkv import B200Backend, CacheConfig
+    from pagedkv.driver import DeviceStepper
+    from pagedkv.traces import beam_cow_trace, churn_trace
+
+    args, world, dev, stream = run.args, run.world, run.dev, run.stream
+    W, K = args.warmup, args.steps
+    if kind == "cow":
+        cfg = CacheConfig(num_blocks=BLOCKS_PER_CHUNK, **GEOM)
+        plans = list(beam_cow_trace(cfg, groups=64, width=4, prefix=2048, steps=W + K,
+                                    zero_per_step=64, seed=0))
+        rows = 64 * 2048
+        workload = ("beam search: 64 prefixes of 2048 tokens forked to 4 beams; every step "
+                    "re-forks 4 children per group from seeded parents and appends one token to "
+                    "each (copy-on-write of the shared tail), frees the old beams, zeroes 64 freed "
+                    "blocks; Qwen2-7B KV geometry, 32,768-block pool")
+    else:
+        heads, hd, layers = 8, 128, 80
+        per_gpu = 150e9
+        nb = int(per_gpu // (layers * 2 * 16 * (heads * hd // world) * 2))
+        cfg = CacheConfig(num_blocks=nb, block_size=16, num_kv_heads=heads, head_dim=hd,
+                          num_layers=layers, dtype_bytes=2)
+        plans = list(churn_trace(cfg, steps=W + K, arrival_rate=8.0, prompt_lo=64,
+                                 prompt_hi=8192, out_mean=256.0, max_batch=4096,
+                                 fork_rate=args.fork_rate, zero_freed=False, seed=0))
+        rows = 16384
+        workload = (f"continuous batching: Poisson(8) arrivals per step, prompts log-uniform "
+                    f"[64, 8192], outputs geometric mean 256, max batch 4096, recompute "
+                    f"preemption, forks of a running sequence with probability {args.fork_rate} "
+                    f"per step; 80 layers, 8 KV heads x 128, bs 16, pool {nb} blocks "
+                    f"(150 GB per GPU); per step: copy_blocks, slot resolution of admitted "
+                    f"prompts, all-layer reshape_and_cache (freed blocks are not zeroed: the "
+                    f"reference marks zero_block a debugging aid)")
+    backend = B200Backend(cfg, dtype="bf16", device=run.local, shard_rank=run.rank, num_shards=world)
+    es, L = backend.shard_entry_elems, cfg.num_layers
+    gen = torch.Generator(device=dev).manual_seed(2000 + run.rank)
+    k = torch.randn((L, rows, es), generator=gen, device=dev, dtype=torch.bfloat16)
+    v = torch.randn((L, rows, es), generator=gen, device=dev, dtype=torch.bfloat16)
+    stepper = DeviceStepper(backend, stream=stream, timing=False)
+    with torch.cuda.stream(stream):
+        for p in plans[: 1 + W if kind == "cow" else W]:
+            stepper.apply(p, k, v)
+    run.barrier()
+    timed = plans[1 + W:] if kind == "cow" else plans[W:]
+    stepper.timing = True
+    run.barrier()
+    with ClockSampler(run.local) as clocks:
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            for p in timed:
+                stepper.apply(p, k, v)
+        run.barrier()
+        host_s = time.perf_counter() - t0
+    ph = stepper.phase_ms()
+    if backend.device_error() is not None:
+        raise SystemExit(f"device error in trace: {backend.device_error()}")
+    total = run.max_over_ranks(ph["total"])
+    tokens = sum(p.num_tokens for p in timed)
+    copies = sum(len(p.copies) for p in timed)
+    zeros = sum(len(p.zero) for p in timed)
+    eb, bb = es * 2, cfg.block_size * es * 2
+    copy_bytes = copies * L * 2 * bb * 2 + 16 * copies
+    write_bytes = tokens * L * 2 * eb * 2 + 8 * tokens
+    zero_bytes = zeros * L * 2 * bb + 8 * zeros
+    phase = {p: run.max_over_ranks(ph[p]) for p in stepper.PHASES}
+    out = base_line(run, tokens / (total / 1e3), len(timed), total / len(timed), "strong", workload, {
+        "steps_timed": len(timed), "warmup_steps": W, "layers": L, "entry_elems_per_gpu": es,
+        "pool_gib_per_gpu": round(backend.allocated_bytes() / 2**30, 2),
+        "parallelism": f"kv-head shards x{world}", "tokens_written": tokens,
+        "copy_pairs": copies, "zeroed_blocks": zeros,
+        "l2": "copies and writes stream through far more than the 126 MB L2 over the trace",
+    }, "synthetic (seeded host trace through the native BlockAllocator/BlockTable/Scheduler)")
+    out["gb_per_s"] = (copy_bytes + write_bytes + zero_bytes) * world / (total / 1e3) / 1e9
+    out["phases_ms"] = phase
+    out["phase_gb_per_s"] = {
+        "copy_blocks": copy_bytes / (phase["copy_blocks"] / 1e3) / 1e9 if phase["copy_blocks"] else None,
+        "reshape_and_cache": write_bytes / (phase["reshape_and_cache"] / 1e3) / 1e9,
+        "zero_blocks": zero_bytes / (phase["zero_blocks"] / 1e3) / 1e9 if phase["zero_blocks"] else None,
+    }
+    if kind == "cow":
+        out["roofline"] = roofline("copy_blocks_kernel (256 pairs x 28 layers per step)",
+                                   copy_bytes / len(timed), phase["copy_blocks"] / len(timed))
+    else:
+        out["roofline"] = roofline("reshape_copy_kernel (all layers)", write_bytes / len(timed),
+                                   phase["reshape_and_cache"] / len(timed))
+        st = [p.stats for p in timed]
+        out["trace"] = {"admitted": sum(s["admitted"] for s in st),
+                        "preempted": sum(s["preempted"] for s in st),
+                        "finished": sum(s["finished"] for s in st),
+                        "rejected": st[-1]["rejected"],
+                        "running_final": st[-1]["running"],
+                        "utilization_max": max(s["utilization"] for s in st)}
+    out["host_driver_s"] = host_s
+    out["gpu_launches"] = stepper.launches
+    out["clocks"] = {**clocks.summary(), "window": "sampled every 200 ms over the timed trace"}
+    backend.close()
+    return out
+
+
+def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks):
     """Same step through the C ABI's KvBackend entry points with host buffers:
     per layer pkv_write_kv_batch from pinned bf16 rows (host->device copies in
     the timed region), then the device error word read back."""
@@ -567,8 +759,15 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    run = Run(args)
+    if args.workload in ("prefill", "decode"):
+        out = wl_table_batch(run, args.workload)
     else:
-        run_ours(args)
+        out = wl_trace(run, args.workload)
+    run.close()
+    if run.rank == 0:
+        print(json.dumps(out), flush=True)
 
 
 if __name__ == "__main__":

@@ -61,7 +61,12 @@ class _Staging:
 
 
 class DeviceStepper:
-    def __init__(self, backend: B200Backend, stream=None):
+    """Runs StepPlans on `backend`. With timing=True each step also records
+    CUDA events around its four phases; ``phase_ms()`` sums them."""
+
+    PHASES = ("copy_blocks", "resolve_slots", "reshape_and_cache", "zero_blocks")
+
+    def __init__(self, backend: B200Backend, stream=None, timing: bool = False):
         import torch
 
         self.torch = torch
@@ -72,6 +77,28 @@ class DeviceStepper:
         self.slots = torch.empty(0, dtype=torch.int64, device=self.dev)
         self.cu = torch.empty(0, dtype=torch.int32, device=self.dev)
         self.launches = 0
+        self.timing = timing
+        self.events: list[list] = []
+
+    def _mark(self, marks: list) -> None:
+        if self.timing:
+            e = self.torch.cuda.Event(enable_timing=True)
+            e.record(self.stream)
+            marks.append(e)
+
+    def phase_ms(self) -> dict:
+        """Summed milliseconds per phase and in total over the recorded steps."""
+        self.stream.synchronize()
+        out = {p: 0.0 for p in self.PHASES}
+        for m in self.events:
+            for i, p in enumerate(self.PHASES):
+                out[p] += m[i].elapsed_time(m[i + 1])
+        if self.events:
+            out["total"] = self.events[0][0].elapsed_time(self.events[-1][-1])
+        return out
+
+    def reset_timing(self) -> None:
+        self.events = []
 
     def _ensure(self, t: int, s: int):
         torch = self.torch
@@ -97,9 +124,12 @@ class DeviceStepper:
         d_copies, d_tables, d_ctx, d_new, d_direct, d_zero = self.stage.upload(
             [copies, tables, ctx, new, direct, zero], st)
         n = 0
+        marks: list = []
+        self._mark(marks)
         if len(copies):
             b.copy_blocks_dev(d_copies, count=len(copies), stream=st)
             n += 1
+        self._mark(marks)
         if s:
             b.resolve_slots(d_tables.view(torch.int32)[: tables.size].view(tables.shape),
                             d_ctx.view(torch.int32)[:s], d_new.view(torch.int32)[:s], tr,
@@ -108,14 +138,19 @@ class DeviceStepper:
         if d:
             with torch.cuda.stream(st):
                 self.slots[tr:t].copy_(d_direct[:d], non_blocking=True)
+        self._mark(marks)
         rows = k.shape[1]
         for c0 in range(0, t, rows):
             c = min(rows, t - c0)
             b.reshape_and_cache(k[:, :c], v[:, :c], self.slots[c0:c0 + c], stream=st)
             n += 1
+        self._mark(marks)
         if len(zero):
             b.zero_blocks_dev(d_zero, count=len(zero), stream=st)
             n += 1
+        self._mark(marks)
+        if self.timing:
+            self.events.append(marks)
         self.launches += n
         return n
 

@@ -131,7 +131,8 @@ def beam_cow_trace(cfg: CacheConfig, groups: int = 64, width: int = 4, prefix: i
 
 def churn_trace(cfg: CacheConfig, steps: int = 2000, arrival_rate: float = 8.0,
                 prompt_lo: int = 64, prompt_hi: int = 8192, out_mean: float = 256.0,
-                max_batch: int = 4096, fork_rate: float = 0.0, seed: int = 0):
+                max_batch: int = 4096, fork_rate: float = 0.0, zero_freed: bool = True,
+                seed: int = 0):
     """Continuous batching through Scheduler::step (scheduler.rs:218-226):
     Poisson(arrival_rate) arrivals per step with log-uniform prompt lengths
     in [prompt_lo, prompt_hi] and geometric output lengths of mean
@@ -141,7 +142,8 @@ def churn_trace(cfg: CacheConfig, steps: int = 2000, arrival_rate: float = 8.0,
 
     Each step's plan writes the prompts of sequences admitted (and not
     preempted again) this step, resolved on the device from their tables,
-    then every decoded token at the slot the scheduler returned."""
+    then every decoded token at the slot the scheduler returned, and (with
+    zero_freed) zeroes every block the step released."""
     sched = Scheduler(cfg.num_blocks, cfg.block_size, max_batch)
     bs = cfg.block_size
     st = Stream(seed)
@@ -179,8 +181,8 @@ def churn_trace(cfg: CacheConfig, steps: int = 2000, arrival_rate: float = 8.0,
         yield StepPlan(copies, _pack_tables(rows) if rows else np.zeros((0, 1), np.int32),
                        np.zeros(len(new), np.int32), np.asarray(new, np.int32),
                        (r["decoded_block"] * bs + r["decoded_slot"]).astype(np.int64),
-                       r["freed"].astype(np.int64),
-                       {"step": step, "admitted": len(r["admitted"]), "preempted": len(pre),
+                       r["freed"].astype(np.int64) if zero_freed else np.zeros(0, np.int64),
+                       {"step": step, "freed": len(r["freed"]), "admitted": len(r["admitted"]), "preempted": len(pre),
                         "finished": len(fin), "running": sched.num_running(),
                         "waiting": sched.num_waiting(), "rejected": rejected,
                         "utilization": sched.pool_utilization()})

@@ -194,13 +194,14 @@ def _tables_from_order(order: np.ndarray, admit_blocks: np.ndarray, extra: np.nd
 
 
 def decode_batch(seed: int | None = None, num_seqs: int = 256, max_ctx: int = 4096,
-                 num_blocks: int = 32768, cfg: CacheConfig | None = None) -> Batch:
+                 num_blocks: int = 32768, cfg: CacheConfig | None = None,
+                 first_seed: int = 0) -> Batch:
     """Config 2: every sequence has ctx ~ U{1..max_ctx} cached tokens and
-    appends one. With seed None the first seed >= 0 whose demand fits the
-    pool is used (roughly half of all seeds overflow 32768 blocks)."""
+    appends one. With seed None the first seed >= first_seed whose demand
+    fits the pool is used (roughly half of all seeds overflow 32768 blocks)."""
     cfg = cfg or CacheConfig(num_blocks=num_blocks, **QWEN2_7B)
     bs = cfg.block_size
-    s0 = 0 if seed is None else seed
+    s0 = first_seed if seed is None else seed
     for sd in range(s0, s0 + 10_000):
         st = Stream(sd)
         ctx = st.integers(num_seqs, 1, max_ctx)
