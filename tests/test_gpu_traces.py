@@ -66,7 +66,7 @@ def test_decode_step_from_a_shuffled_allocator(cuda):  # config 2 at reduced geo
 def test_ragged_prefill_chunk(cuda):  # config 3 at reduced geometry
     cfg = CacheConfig(num_blocks=1024, block_size=16, num_kv_heads=2, head_dim=32, num_layers=3,
                       dtype_bytes=2)
-    batch = prefill_chunk(seed=3, num_prompts=12, lo=16, hi=900, budget=3000, cfg=cfg)
+    batch = prefill_chunk(seed=3, num_prompts=24, lo=16, hi=900, budget=3000, cfg=cfg)
     assert batch.num_tokens == 3000
     run(cfg, [plan_from_batch(batch)], r=4096)
 
