@@ -512,7 +512,13 @@ def wl_trace(run, kind: str) -> dict:
     timed = plans[1 + W:] if kind == "cow" else plans[W:]
     stepper.timing = True
     run.barrier()
+    busy = torch.ones(2**30, dtype=torch.uint8, device=dev)
     with ClockSampler(run.local) as clocks:
+        # A second of streaming reads first, so the clock samples see the GPU under load.
+        t_load = time.perf_counter()
+        while time.perf_counter() - t_load < 1.0:
+            busy.sum(dtype=torch.int64)
+            torch.cuda.synchronize()
         t0 = time.perf_counter()
         with torch.cuda.stream(stream):
             for p in timed:
@@ -560,7 +566,8 @@ def wl_trace(run, kind: str) -> dict:
                         "utilization_max": max(s["utilization"] for s in st)}
     out["host_driver_s"] = host_s
     out["gpu_launches"] = stepper.launches
-    out["clocks"] = {**clocks.summary(), "window": "sampled every 200 ms over the timed trace"}
+    out["clocks"] = {**clocks.summary(),
+                     "window": "sampled every 200 ms over 1 s of streaming reads and the timed trace"}
     backend.close()
     return out
 

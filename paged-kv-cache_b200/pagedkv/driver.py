@@ -3,7 +3,8 @@
 One step issues, on one CUDA stream and in the order the scheduler's
 contract requires (crates/paged-kv-core/src/scheduler.rs:57-63):
 
-1. copy_blocks of the step's copy-on-write pairs,
+1. copy_blocks of the step's copy-on-write pairs (in dependency waves, so
+   pairs that chain within the step keep their sequential meaning),
 2. slot resolution for the sequences given as block tables,
 3. one all-layer reshape_and_cache for every new token,
 4. zero_blocks of the blocks freed this step.
@@ -58,6 +59,40 @@ class _Staging:
             out.append(self.device[off: off + w])
             off += w
         return out
+
+
+def copy_waves(copies: np.ndarray):
+    """Orders a step's copy pairs into waves that may each run fully in
+    parallel and, applied one after another, give the result of applying
+    the pairs sequentially (the trait's default copy_blocks loop,
+    crates/paged-kv-core/src/backend.rs:104-109).
+
+    Copy-on-write pairs within one scheduler step can chain: a block freed
+    earlier in the step (an old beam, a preempted sequence) can come back
+    off the free list as a later pair's destination while an earlier pair
+    still reads it as its source. A pair goes one wave after every earlier
+    pair that writes its source, reads its destination or writes its
+    destination. Self-copies are dropped. Returns (ordered pairs [P'][2],
+    [(start, count)] per wave)."""
+    last_write: dict[int, int] = {}
+    last_read: dict[int, int] = {}
+    keep, wave = [], []
+    for i, (src, dst) in enumerate(copies.tolist()):
+        if src == dst:
+            continue
+        w = max(last_write.get(src, -1), last_read.get(dst, -1), last_write.get(dst, -1)) + 1
+        last_write[dst] = w
+        last_read[src] = max(last_read.get(src, -1), w)
+        keep.append(i)
+        wave.append(w)
+    if not keep:
+        return np.zeros((0, 2), np.int64), []
+    wave = np.asarray(wave)
+    order = np.argsort(wave, kind="stable")
+    ordered = np.ascontiguousarray(copies[np.asarray(keep)[order]], dtype=np.int64)
+    counts = np.bincount(wave)
+    starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    return ordered, [(int(a), int(c)) for a, c in zip(starts, counts) if c]
 
 
 class DeviceStepper:
@@ -116,18 +151,18 @@ class DeviceStepper:
         t, s = tr + d, len(plan.new)
         self._ensure(t, s)
         tables = np.ascontiguousarray(plan.tables, np.int32)
-        copies, ctx, new, direct, zero = (np.ascontiguousarray(plan.copies, np.int64),
-                                          np.ascontiguousarray(plan.ctx, np.int32),
-                                          np.ascontiguousarray(plan.new, np.int32),
-                                          np.ascontiguousarray(plan.direct_slots, np.int64),
-                                          np.ascontiguousarray(plan.zero, np.int64))
+        copies, waves = copy_waves(np.asarray(plan.copies, np.int64).reshape(-1, 2))
+        ctx = np.ascontiguousarray(plan.ctx, np.int32)
+        new = np.ascontiguousarray(plan.new, np.int32)
+        direct = np.ascontiguousarray(plan.direct_slots, np.int64)
+        zero = np.ascontiguousarray(plan.zero, np.int64)
         d_copies, d_tables, d_ctx, d_new, d_direct, d_zero = self.stage.upload(
             [copies, tables, ctx, new, direct, zero], st)
         n = 0
         marks: list = []
         self._mark(marks)
-        if len(copies):
-            b.copy_blocks_dev(d_copies, count=len(copies), stream=st)
+        for start, count in waves:
+            b.copy_blocks_dev(d_copies[2 * start:], count=count, stream=st)
             n += 1
         self._mark(marks)
         if s:
