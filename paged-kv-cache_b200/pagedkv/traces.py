@@ -83,7 +83,8 @@ def _pack_tables(rows: list[np.ndarray]) -> np.ndarray:
 
 
 def beam_cow_trace(cfg: CacheConfig, groups: int = 64, width: int = 4, prefix: int = 2048,
-                   steps: int = 100, zero_per_step: int = 64, seed: int = 0):
+                   steps: int = 100, zero_per_step: int = 64, seed: int = 0,
+                   interleave: bool = False):
     """Beam search over shared prefixes.
 
     Step 0 prefills `groups` prefixes of `prefix` tokens and forks each to
@@ -92,7 +93,14 @@ def beam_cow_trace(cfg: CacheConfig, groups: int = 64, width: int = 4, prefix: i
     the children from them, appends one token to every child while the old
     beams are still alive -- so each append onto a partly filled tail is a
     copy-on-write (block_table.rs:135-150) -- then frees the old beams and
-    zeroes up to `zero_per_step` of the blocks that freeing released."""
+    zeroes up to `zero_per_step` of the blocks that freeing released.
+
+    By default the step forks and appends for every group before it frees
+    any old beam, as a batched engine does; blocks freed in a step are then
+    reused only by later steps. With interleave=True each group frees its old
+    beams before the next group appends, so the LIFO free list hands a block
+    that an earlier pair of the same step copied from to a later pair as its
+    destination: the step's copy list chains."""
     a = BlockAllocator(cfg.num_blocks)
     bs = cfg.block_size
     st = Stream(seed)
@@ -109,6 +117,7 @@ def beam_cow_trace(cfg: CacheConfig, groups: int = 64, width: int = 4, prefix: i
                    {"step": 0, "copies": 0})
     for step in range(1, steps + 1):
         copies, slots, old = [], [], []
+        retired = []
         for g in range(groups):
             parents = st.integers(width, 0, width - 1)
             children = [beams[g][int(p)].fork(a) for p in parents]
@@ -117,10 +126,16 @@ def beam_cow_trace(cfg: CacheConfig, groups: int = 64, width: int = 4, prefix: i
                 if cow is not None:
                     copies.append(cow)
                 slots.append(slot.block * bs + slot.slot)
-            for t in beams[g]:
+            retired.append(beams[g])
+            beams[g] = children
+            if interleave:
+                for t in retired.pop():
+                    old.append(t.physical_blocks())
+                    t.free(a)
+        for group in retired:
+            for t in group:
                 old.append(t.physical_blocks())
                 t.free(a)
-            beams[g] = children
         cand = np.unique(np.concatenate([np.asarray(o, np.int64) for o in old]))
         freed = cand[a.ref_counts(cand) == 0]
         ti, ci, ni = _empty_tables()

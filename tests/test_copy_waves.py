@@ -51,7 +51,8 @@ def test_beam_trace_chains_within_a_step_and_waves_keep_its_meaning():
     cfg = CacheConfig(num_blocks=512, block_size=8, num_kv_heads=1, head_dim=1, num_layers=1,
                       dtype_bytes=2)
     chained = 0
-    for plan in beam_cow_trace(cfg, groups=6, width=4, prefix=37, steps=30, zero_per_step=5, seed=2):
+    for plan in beam_cow_trace(cfg, groups=6, width=4, prefix=37, steps=30, zero_per_step=5, seed=2,
+                               interleave=True):
         if not len(plan.copies):
             continue
         waves = copy_waves(plan.copies)[1]
@@ -60,3 +61,11 @@ def test_beam_trace_chains_within_a_step_and_waves_keep_its_meaning():
         np.testing.assert_array_equal(by_waves(pool.copy(), plan.copies),
                                       sequential(pool.copy(), plan.copies))
     assert chained > 0  # freeing old beams group by group does chain copies within a step
+
+
+def test_batched_beam_steps_do_not_chain():
+    cfg = CacheConfig(num_blocks=4096, block_size=16, num_kv_heads=1, head_dim=1, num_layers=1,
+                      dtype_bytes=2)
+    for plan in beam_cow_trace(cfg, groups=16, width=4, prefix=100, steps=20, seed=1):
+        if len(plan.copies):
+            assert len(copy_waves(plan.copies)[1]) == 1

@@ -71,10 +71,14 @@ def test_ragged_prefill_chunk(cuda):  # config 3 at reduced geometry
     run(cfg, [plan_from_batch(batch)], r=4096)
 
 
-def test_beam_search_copy_on_write_trace(cuda):  # config 4 at reduced geometry
+@pytest.mark.parametrize("interleave", [False, True])
+def test_beam_search_copy_on_write_trace(cuda, interleave):  # config 4 at reduced geometry
+    """interleave=True frees old beams group by group, which chains copy
+    pairs within a step; the driver must keep their sequential meaning."""
     cfg = CacheConfig(num_blocks=512, block_size=8, num_kv_heads=2, head_dim=16, num_layers=3,
                       dtype_bytes=2)
-    plans = list(beam_cow_trace(cfg, groups=6, width=4, prefix=37, steps=30, zero_per_step=5, seed=2))
+    plans = list(beam_cow_trace(cfg, groups=6, width=4, prefix=37, steps=30, zero_per_step=5, seed=2,
+                                interleave=interleave))
     stats = run(cfg, plans, r=512, check_every=7)
     copies = sum(s["copies"] for s in stats)
     # Every child pays a copy except on steps whose append opens a new block.
