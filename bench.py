@@ -72,25 +72,31 @@ def parse():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons of the GPUs in `indices`
+    while the timed region runs. One process (rank 0) samples every GPU of
+    the job; it waits for the first sample before the load starts."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, indices, active: bool = True):
+        self.indices = list(indices)
+        self.active = active
         self.proc = None
         self.lines: list[str] = []
+        self.first = threading.Event()
 
     def __enter__(self):
+        if not self.active:
+            return self
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", "-i", ",".join(str(i) for i in self.indices),
+                 f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+            threading.Thread(target=self._read, daemon=True).start()
+            self.first.wait(timeout=20.0)
         except OSError:
             self.proc = None
         return self
@@ -98,6 +104,7 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+            self.first.set()
 
     def __exit__(self, *exc):
         if self.proc:
@@ -123,7 +130,7 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "gpus": self.indices}
 
 
 def measured_peak_gbs() -> tuple[float, str]:
@@ -242,7 +249,8 @@ class Run:
         torch = self.torch
         evs = []
         self.barrier()
-        with ClockSampler(self.local) as clocks:
+        with ClockSampler(range(self.world), active=self.rank == 0) as clocks:
+            self.barrier()
             self.load(lambda: step(-1, None), 1.0)
             self.barrier()
             start = torch.cuda.Event(enable_timing=True)
@@ -513,7 +521,8 @@ def wl_trace(run, kind: str) -> dict:
     stepper.timing = True
     run.barrier()
     busy = torch.ones(2**30, dtype=torch.uint8, device=dev)
-    with ClockSampler(run.local) as clocks:
+    with ClockSampler(range(world), active=run.rank == 0) as clocks:
+        run.barrier()
         # A second of streaming reads first, so the clock samples see the GPU under load.
         t_load = time.perf_counter()
         while time.perf_counter() - t_load < 1.0:

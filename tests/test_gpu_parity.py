@@ -473,3 +473,61 @@ def test_rows_digest_predicts_the_pool_digest(cuda, src):
             whole = digs[0]
         else:
             assert tuple(sum(d[i] for d in digs) % 2**64 for i in range(2)) == whole
+
+
+def test_offsets_beyond_2_31_elements_per_plane(cuda):
+    """A plane of 80 layers x 2,048 blocks x 16 slots x 1,024 elements holds
+    2.7e9 elements (> 2^31): the last layer's last block must be addressed
+    exactly, through every entry point."""
+    import torch
+
+    cfg = CacheConfig(num_blocks=2048, block_size=16, num_kv_heads=8, head_dim=128, num_layers=80,
+                      dtype_bytes=2)
+    assert cfg.num_layers * cfg.layer_elems() > 2**31
+    b = B200Backend(cfg, dtype="bf16")
+    e = cfg.entry_elems()
+    st = Stream(55)
+    bits = f32_to_bf16_bits(st.normal(2 * 3 * e)).reshape(2, 3, e)
+    dsts = [(2047, 15), (2047, 0), (1500, 7)]
+    b.write_kv_batch(79, dsts, bits[0].ravel(), bits[1].ravel(), host_dtype="bf16")
+    for i, d in enumerate(dsts):
+        k = np.zeros(e, np.uint16)
+        v = np.zeros(e, np.uint16)
+        b.read_kv(79, d, k, v)
+        assert (k == bits[0, i]).all() and (v == bits[1, i]).all()
+    b.copy_blocks([(2047, 2046)])
+    k = np.zeros(e, np.uint16)
+    b.read_kv(79, (2046, 15), k, np.zeros(e, np.uint16))
+    assert (k == bits[0, 0]).all()
+    # Device path, all layers, into the last block.
+    rows = torch.randn((80, 2, e), device=cuda).to(torch.bfloat16)
+    slots = torch.tensor([2047 * 16 + 3, 2047 * 16 + 4], dtype=torch.int64, device=cuda)
+    b.reshape_and_cache(rows, rows, slots)
+    pk, _ = b.planes()
+    assert torch.equal(pk[79, 2047, 3:5], rows[79])
+    assert torch.equal(pk[0, 2047, 3:5], rows[0])
+    b.zero_blocks([2047])
+    assert int(torch.count_nonzero(pk[:, 2047])) == 0
+    assert b.device_error() is None
+
+
+def test_empty_device_calls_launch_nothing_and_succeed(cuda):
+    import torch
+
+    b = B200Backend(CacheConfig(8, 4, 1, 8, 2, 2), dtype="bf16")
+    z64 = torch.zeros(0, dtype=torch.int64, device=cuda)
+    e = torch.zeros((0, 8), dtype=torch.bfloat16, device=cuda)
+    b.reshape_and_cache(e, e, z64, layer=0)
+    b.copy_blocks_dev(z64.view(0, 2) if z64.numel() else torch.zeros((0, 2), dtype=torch.int64, device=cuda))
+    b.zero_blocks_dev(z64)
+    b.write_kv_batch(1, [], np.zeros(0, np.float32), np.zeros(0, np.float32))
+    b.copy_blocks([])
+    b.zero_blocks([])
+    cu = torch.full((1,), 7, dtype=torch.int32, device=cuda)
+    z32 = torch.zeros(0, dtype=torch.int32, device=cuda)
+    b.resolve_slots(torch.zeros((0, 1), dtype=torch.int32, device=cuda), z32, z32, 0, cu,
+                    torch.zeros(1, dtype=torch.int64, device=cuda))
+    torch.cuda.synchronize()
+    assert cu.item() == 0 and b.device_error() is None
+    pk, pv = b.planes()
+    assert int(torch.count_nonzero(pk)) == 0 and int(torch.count_nonzero(pv)) == 0
