@@ -54,6 +54,8 @@ def parse():
     p.add_argument("--fork-rate", type=float, default=0.05,
                    help="churn: probability per step of forking a running sequence")
     p.add_argument("--no-graph", action="store_true", help="decode: launch instead of graph replay")
+    p.add_argument("--unfused", action="store_true",
+                   help="resolve slots and scatter in two launches instead of the fused kernel")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-ops", action="store_true")
@@ -339,8 +341,12 @@ def wl_table_batch(run, kind: str) -> dict:
     d_slots = torch.empty(T, dtype=torch.int64, device=dev)
 
     def launch():
-        backend.resolve_slots(d_tab, d_ctx, d_new, T, d_cu, d_slots, stream=stream)
-        backend.reshape_and_cache(k, v, d_slots, stream=stream)
+        if args.unfused:
+            backend.resolve_slots(d_tab, d_ctx, d_new, T, d_cu, d_slots, stream=stream)
+            backend.reshape_and_cache(k, v, d_slots, stream=stream)
+        else:  # one launch: slots resolved inline, also published to d_slots
+            backend.resolve_and_cache(d_tab, d_ctx, d_new, T, d_cu, k, v, slots_out=d_slots,
+                                      stream=stream)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -362,7 +368,7 @@ def wl_table_batch(run, kind: str) -> dict:
         if graph is not None:
             graph.replay()
             return
-        if ev is not None:
+        if ev is not None and args.unfused:
             for _ in range(3):
                 ev.append(torch.cuda.Event(enable_timing=True))
             ev[0].record(stream)
@@ -370,6 +376,12 @@ def wl_table_batch(run, kind: str) -> dict:
             ev[1].record(stream)
             backend.reshape_and_cache(k, v, d_slots, stream=stream)
             ev[2].record(stream)
+        elif ev is not None:
+            for _ in range(2):
+                ev.append(torch.cuda.Event(enable_timing=True))
+            ev[0].record(stream)
+            launch()
+            ev[1].record(stream)
         else:
             launch()
 
@@ -377,24 +389,25 @@ def wl_table_batch(run, kind: str) -> dict:
     total_ms, evs, clocks = run.timed_steps(step, K)
     eb = es * 2
     alg_bytes = T * L * 2 * eb * 2 + T * 8  # read + write K and V, one slot read per token
-    if graph is None:
-        reshape_ms = run.max_over_ranks(_event_ms(evs, 1, 2))
+    if graph is None and args.unfused:
+        kernel_ms = run.max_over_ranks(_event_ms(evs, 1, 2))
         resolve_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
+    elif graph is None:
+        kernel_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
+        resolve_ms = 0.0
     else:
-        # Kernel time of the graph's reshape: the same launch timed on its own.
+        # Kernel time inside the graph: the same launch timed on its own.
         evs2 = []
         with torch.cuda.stream(stream):
             for _ in range(max(K, 10)):
-                e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
                 e[0].record(stream)
-                backend.resolve_slots(d_tab, d_ctx, d_new, T, d_cu, d_slots, stream=stream)
+                launch()
                 e[1].record(stream)
-                backend.reshape_and_cache(k, v, d_slots, stream=stream)
-                e[2].record(stream)
                 evs2.append(e)
         stream.synchronize()
-        reshape_ms = run.max_over_ranks(_event_ms(evs2, 1, 2))
-        resolve_ms = run.max_over_ranks(_event_ms(evs2, 0, 1))
+        kernel_ms = run.max_over_ranks(_event_ms(evs2, 0, 1))
+        resolve_ms = 0.0 if not args.unfused else None
 
     verify = verify_over_group(backend.digest(stream=stream),
                                backend.digest_rows(k, v, d_slots, stream=stream), device=dev)
@@ -410,7 +423,8 @@ def wl_table_batch(run, kind: str) -> dict:
         workload = f"decode step x{world}: {world}x256 sequences, context U[1,4096], +1 token each"
     workload += (f", Qwen2-7B KV geometry (28 layers, 4 KV heads x 128, bs 16), pool "
                  f"{cfg.num_blocks} blocks (shuffled free list) head-sharded {world} ways; step = "
-                 "device slot resolution + all-layer reshape_and_cache"
+                 + ("device slot resolution + all-layer reshape_and_cache" if args.unfused else
+                  "slot resolution fused with the all-layer reshape_and_cache (one launch)")
                  + (" replayed as one CUDA graph" if graph is not None else ""))
     out = base_line(run, T * K / (total_ms / 1e3), K, total_ms / K, "weak", workload, {
         "tokens_per_step": T, "sequences_per_step": S, "layers": L, "entry_elems_per_gpu": es,
@@ -423,10 +437,13 @@ def wl_table_batch(run, kind: str) -> dict:
     }, "synthetic (seeded: shuffled free list, " + ("log-uniform prompt lengths" if kind == "prefill"
                                                        else "uniform context lengths") + ", normal K/V)")
     out["gb_per_s"] = alg_bytes * world / (total_ms / K / 1e3) / 1e9
-    out["roofline"] = roofline("reshape_copy_kernel (all layers)", alg_bytes, reshape_ms,
+    kname = ("reshape_copy_kernel (all layers)" if args.unfused else
+             "resolve_cache_kernel (slot resolution fused with the all-layer reshape_and_cache)")
+    out["roofline"] = roofline(kname, alg_bytes, kernel_ms,
                                profile_traffic("reshape_prefill_ncu") if kind == "prefill" else None)
-    out["resolve_slots_ms"] = resolve_ms
-    out["gpu_launches"] = 2 * K
+    if args.unfused:
+        out["resolve_slots_ms"] = resolve_ms
+    out["gpu_launches"] = (2 if args.unfused else 1) * K
     out["verify"] = verify
     out["clocks"] = clocks
     if kind == "prefill" and not args.no_ops and run.rank == 0:
@@ -438,8 +455,7 @@ def wl_table_batch(run, kind: str) -> dict:
         n = min(4096, T)
         out["cpu_baseline"] = cpu_sample(tables, ctx, new, k[:, :n].float().cpu().numpy(),
                                          v[:, :n].float().cpu().numpy(), seconds=8.0, threads=1)
-    if graph is not None:
-        del graph
+    graph = None  # release the captured graph before its pool is freed
     backend.close()
     return out
 
@@ -555,17 +571,18 @@ def wl_trace(run, kind: str) -> dict:
     }, "synthetic (seeded host trace through the native BlockAllocator/BlockTable/Scheduler)")
     out["gb_per_s"] = (copy_bytes + write_bytes + zero_bytes) * world / (total / 1e3) / 1e9
     out["phases_ms"] = phase
+    write_ms = phase["resolve_and_cache"] + phase["reshape_and_cache"]
     out["phase_gb_per_s"] = {
         "copy_blocks": copy_bytes / (phase["copy_blocks"] / 1e3) / 1e9 if phase["copy_blocks"] else None,
-        "reshape_and_cache": write_bytes / (phase["reshape_and_cache"] / 1e3) / 1e9,
+        "token_writes": write_bytes / (write_ms / 1e3) / 1e9 if write_ms else None,
         "zero_blocks": zero_bytes / (phase["zero_blocks"] / 1e3) / 1e9 if phase["zero_blocks"] else None,
     }
     if kind == "cow":
         out["roofline"] = roofline("copy_blocks_kernel (256 pairs x 28 layers per step)",
                                    copy_bytes / len(timed), phase["copy_blocks"] / len(timed))
     else:
-        out["roofline"] = roofline("reshape_copy_kernel (all layers)", write_bytes / len(timed),
-                                   phase["reshape_and_cache"] / len(timed))
+        out["roofline"] = roofline("resolve_cache_kernel + reshape_copy_kernel (token writes, all "
+                                   "layers)", write_bytes / len(timed), write_ms / len(timed))
         st = [p.stats for p in timed]
         out["trace"] = {"admitted": sum(s["admitted"] for s in st),
                         "preempted": sum(s["preempted"] for s in st),

@@ -169,6 +169,18 @@ int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t t
                           const int32_t *ctx_lens, const int32_t *new_lens, int64_t num_seqs,
                           int64_t num_tokens, int32_t *cu_seqlens, int64_t *slot_mapping,
                           void *stream);
+/* Slot resolution fused with reshape_and_cache: one launch per step, the
+ * slots computed inline (no slot_mapping round trip through memory). Same
+ * arguments and results as pkv_resolve_slots_dev followed by
+ * pkv_reshape_and_cache_dev(layer, k, v, ...); slot_mapping is an optional
+ * output (NULL: not written) for kernels that read the cache afterwards.
+ * src_dtype must equal the pool dtype. */
+int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64_t table_stride,
+                              const int32_t *ctx_lens, const int32_t *new_lens, int64_t num_seqs,
+                              int64_t num_tokens, int32_t *cu_seqlens, int64_t *slot_mapping,
+                              int64_t layer, const void *k, const void *v,
+                              int64_t src_token_stride, int64_t src_layer_stride, int src_dtype,
+                              void *stream);
 /* Order-independent 64-bit digests of this backend's K and V planes (the
  * element's global index in the full plane and its f32-widened bits, summed;
  * zeros contribute nothing). Digests of the shards of one pool add up

@@ -628,6 +628,68 @@ Status B200Backend::resolve_slots_dev(const int32_t *tables, int64_t table_strid
     return check("resolve_slots", launch_resolve_slots(a, sms_, st));
 }
 
+Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_stride,
+                                          const int32_t *ctx, const int32_t *new_lens,
+                                          int64_t num_seqs, int64_t num_tokens, int32_t *cu,
+                                          int64_t *slots_out, int64_t layer, const void *k,
+                                          const void *v, int64_t tok_stride,
+                                          int64_t layer_stride, DType src, cudaStream_t st) {
+    if (layer < -1 || (layer >= 0 && (uint64_t)layer >= cfg_.num_layers))
+        return error(PKV_ERR_INVALID_LAYER, layer, (int64_t)cfg_.num_layers,
+                     msg_layer((uint64_t)layer, cfg_.num_layers));
+    if (num_seqs < 0 || num_tokens < 0 || table_stride < 0)
+        return error(PKV_ERR_SHAPE_MISMATCH, 0, std::min({num_seqs, num_tokens, table_stride}),
+                     "negative size");
+    if (num_seqs > kMaxResolveSeqs)
+        return error(PKV_ERR_DEVICE, 0, 0,
+                     "slot resolution handles at most " + std::to_string(kMaxResolveSeqs) +
+                         " sequences per call");
+    if (num_tokens > std::numeric_limits<int32_t>::max())
+        return error(PKV_ERR_SHAPE_MISMATCH, std::numeric_limits<int32_t>::max(), num_tokens,
+                     "too many tokens for int32 cu_seqlens");
+    if (src != dtype_)
+        return error(PKV_ERR_DEVICE, 0, 0,
+                     "the fused path moves bytes: source dtype must equal the pool dtype "
+                     "(use pkv_resolve_slots_dev + pkv_reshape_and_cache_dev to convert)");
+    if (!cu || (num_seqs > 0 && (!ctx || !new_lens)) ||
+        (num_tokens > 0 && (!tables || !k || !v)))
+        return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    if (tok_stride <= 0) tok_stride = (int64_t)shard_entry_;
+    if ((uint64_t)tok_stride < shard_entry_)
+        return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)shard_entry_, tok_stride,
+                     "token stride shorter than an entry");
+    const bool all = layer == -1;
+    if (all && layer_stride <= 0) layer_stride = tok_stride * num_tokens;
+    if (all && layer_stride < tok_stride * num_tokens)
+        return error(PKV_ERR_SHAPE_MISMATCH, tok_stride * num_tokens, layer_stride,
+                     "layer stride shorter than a layer's rows");
+    DeviceGuard g(device_);
+    const int es = dtype_size(dtype_);
+    ResolveCacheLaunch a{};
+    a.tables = tables;
+    a.table_stride = table_stride;
+    a.ctx_lens = ctx;
+    a.new_lens = new_lens;
+    a.num_seqs = num_seqs;
+    a.num_tokens = num_tokens;
+    a.block_size = (long long)cfg_.block_size;
+    a.num_blocks = (long long)cfg_.num_blocks;
+    a.cu_seqlens = cu;
+    a.slots_out = reinterpret_cast<long long *>(slots_out);
+    a.k = k;
+    a.v = v;
+    a.src_token_stride_bytes = tok_stride * es;
+    a.src_layer_stride_bytes = all ? layer_stride * es : 0;
+    a.k_pool = k_plane_;
+    a.v_pool = v_plane_;
+    a.first_layer = all ? 0 : layer;
+    a.num_layers = all ? (long long)cfg_.num_layers : 1;
+    a.slots_per_layer = (long long)slots_per_layer();
+    a.entry_bytes = (long long)entry_bytes();
+    a.err = d_err_;
+    return check("resolve_and_cache", launch_resolve_cache(a, sms_, st));
+}
+
 Status B200Backend::digest(uint64_t *k, uint64_t *v, cudaStream_t st) {
     DeviceGuard g(device_);
     cudaStream_t s = st;

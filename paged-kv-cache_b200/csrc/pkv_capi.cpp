@@ -196,6 +196,23 @@ int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t t
     });
 }
 
+int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64_t table_stride,
+                              const int32_t *ctx_lens, const int32_t *new_lens, int64_t num_seqs,
+                              int64_t num_tokens, int32_t *cu_seqlens, int64_t *slot_mapping,
+                              int64_t layer, const void *k, const void *v,
+                              int64_t src_token_stride, int64_t src_layer_stride, int src_dtype,
+                              void *stream) {
+    if (!b) return null_handle();
+    if (!valid_dtype(src_dtype)) return bad_dtype();
+    return guarded([&] {
+        return b->impl->resolve_and_cache_dev(block_tables, table_stride, ctx_lens, new_lens,
+                                              num_seqs, num_tokens, cu_seqlens, slot_mapping,
+                                              layer, k, v, src_token_stride, src_layer_stride,
+                                              static_cast<pkv::DType>(src_dtype),
+                                              as_stream(stream));
+    });
+}
+
 int pkv_digest(pkv_backend *b, uint64_t *k_digest, uint64_t *v_digest, void *stream) {
     if (!b || !k_digest || !v_digest) return null_handle();
     return guarded([&] { return b->impl->digest(k_digest, v_digest, as_stream(stream)); });

@@ -88,6 +88,31 @@ struct DigestLaunch {
     unsigned long long *out;   // [2]: K digest, V digest (accumulated)
 };
 
+// Slot resolution fused with reshape_and_cache (same element type in and out).
+struct ResolveCacheLaunch {
+    const int *tables;
+    long long table_stride;
+    const int *ctx_lens;
+    const int *new_lens;
+    long long num_seqs;
+    long long num_tokens;
+    long long block_size;
+    long long num_blocks;
+    int *cu_seqlens;             // [num_seqs + 1], written
+    long long *slots_out;        // [num_tokens] or null
+    const void *k;
+    const void *v;
+    long long src_token_stride_bytes;
+    long long src_layer_stride_bytes;
+    void *k_pool;
+    void *v_pool;
+    long long first_layer;
+    long long num_layers;
+    long long slots_per_layer;
+    long long entry_bytes;
+    DevError *err;
+};
+
 // Digest of rows as a scatter into an empty pool would store them.
 struct DigestRowsLaunch {
     const void *k;
@@ -113,6 +138,7 @@ cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_copy_blocks(const CopyLaunch &a, cudaStream_t s);
 cudaError_t launch_zero_blocks(const ZeroLaunch &a, cudaStream_t s);
 cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t s);
+cudaError_t launch_resolve_cache(const ResolveCacheLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t s);
 

@@ -274,29 +274,24 @@ __device__ __forceinline__ int warp_inclusive_scan(int x) {
     return x;
 }
 
-__global__ void __launch_bounds__(kThreads)
-resolve_slots_kernel(const int *__restrict__ tables, long long table_stride,
-                     const int *__restrict__ ctx, const int *__restrict__ nnew, int num_seqs,
-                     long long num_tokens, long long block_size, long long num_blocks,
-                     int *__restrict__ cu_out, long long *__restrict__ slots, DevError *err) {
-    extern __shared__ int s_cu[];  // num_seqs + 1
-    __shared__ int s_warp[kThreads / 32];
-    __shared__ int s_bad;
+// Exclusive prefix of new_lens into s_cu[0..num_seqs] (one contiguous
+// segment per thread, then warp shuffles); sets *s_bad when a length or a
+// context is negative. Every thread of the CTA must call it.
+__device__ __forceinline__ void scan_lengths(const int *__restrict__ ctx,
+                                             const int *__restrict__ nnew, int num_seqs,
+                                             int *s_cu, int *s_warp, int *s_bad) {
     const int tid = threadIdx.x;
-    if (tid == 0) s_bad = 0;
+    if (tid == 0) *s_bad = 0;
     __syncthreads();
-
-    // Per-thread segment sums.
     const int seg = (num_seqs + kThreads - 1) / kThreads;
     const int b0 = min(num_seqs, tid * seg);
     const int b1 = min(num_seqs, b0 + seg);
     int local = 0;
     for (int q = b0; q < b1; ++q) {
         const int n = __ldg(nnew + q);
-        if (n < 0 || __ldg(ctx + q) < 0) s_bad = 1;
+        if (n < 0 || __ldg(ctx + q) < 0) *s_bad = 1;
         local += max(n, 0);
     }
-    // Block-wide exclusive scan of the segment sums.
     const int incl = warp_inclusive_scan(local);
     if ((tid & 31) == 31) s_warp[tid >> 5] = incl;
     __syncthreads();
@@ -314,6 +309,47 @@ resolve_slots_kernel(const int *__restrict__ tables, long long table_stride,
     if (b1 == num_seqs && b0 < b1) s_cu[num_seqs] = run;
     if (num_seqs == 0 && tid == 0) s_cu[0] = 0;
     __syncthreads();
+}
+
+// Combined slot of packed token t: its sequence by binary search over the
+// prefix, then BlockTable::slot_for_position. -1 (and an error record when
+// `report`) for a logical block past the table or a table entry outside the pool.
+__device__ __forceinline__ long long slot_of_token(long long t, const int *s_cu, int num_seqs,
+                                                   const int *__restrict__ ctx,
+                                                   const int *__restrict__ tables,
+                                                   long long table_stride, long long block_size,
+                                                   long long num_blocks, DevError *err, bool report) {
+    int lo = 0, hi = num_seqs - 1;
+    while (lo < hi) {  // last q with s_cu[q] <= t; that sequence has new_lens > 0
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_cu[mid] <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    const long long pos = (long long)__ldg(ctx + lo) + (t - s_cu[lo]);
+    const long long lb = pos / block_size;
+    const long long off = pos - lb * block_size;
+    if (lb >= table_stride) {
+        if (report) record_error(err, kSlotOutOfRange, t);
+        return -1;
+    }
+    const long long blk = __ldg(tables + (long long)lo * table_stride + lb);
+    if (blk < 0 || blk >= num_blocks) {
+        if (report) record_error(err, kInvalidBlock, t);
+        return -1;
+    }
+    return blk * block_size + off;
+}
+
+__global__ void __launch_bounds__(kThreads)
+resolve_slots_kernel(const int *__restrict__ tables, long long table_stride,
+                     const int *__restrict__ ctx, const int *__restrict__ nnew, int num_seqs,
+                     long long num_tokens, long long block_size, long long num_blocks,
+                     int *__restrict__ cu_out, long long *__restrict__ slots, DevError *err) {
+    extern __shared__ int s_cu[];  // num_seqs + 1
+    __shared__ int s_warp[kThreads / 32];
+    __shared__ int s_bad;
+    const int tid = threadIdx.x;
+    scan_lengths(ctx, nnew, num_seqs, s_cu, s_warp, &s_bad);
 
     const long long total = s_cu[num_seqs];
     if (blockIdx.x == 0) {
@@ -326,25 +362,88 @@ resolve_slots_kernel(const int *__restrict__ tables, long long table_stride,
     if (s_bad || total != num_tokens) return;
 
     const long long stride = (long long)gridDim.x * kThreads;
-    for (long long t = (long long)blockIdx.x * kThreads + tid; t < num_tokens; t += stride) {
-        int lo = 0, hi = num_seqs - 1;
-        while (lo < hi) {  // last q with s_cu[q] <= t; that sequence has new_lens > 0
-            const int mid = (lo + hi + 1) >> 1;
-            if (s_cu[mid] <= t) lo = mid;
-            else hi = mid - 1;
+    for (long long t = (long long)blockIdx.x * kThreads + tid; t < num_tokens; t += stride)
+        slots[t] = slot_of_token(t, s_cu, num_seqs, ctx, tables, table_stride, block_size,
+                                 num_blocks, err, true);
+}
+
+// ---- slot resolution fused with reshape_and_cache ------------------------------
+//
+// One launch per step: every CTA scans new_lens, and each (token, vector)
+// work item resolves its token's slot inline (no slot_mapping round trip
+// through HBM) before moving its vector for every layer of its chunk, as
+// reshape_copy_kernel does. The vector-0 threads of layer chunk 0 also
+// publish the slot (when asked) so attention can use it.
+
+template <typename V, int UNROLL>
+__global__ void __launch_bounds__(kThreads, 4)
+resolve_cache_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
+    extern __shared__ int s_cu[];
+    __shared__ int s_warp[kThreads / 32];
+    __shared__ int s_bad;
+    scan_lengths(a.ctx_lens, a.new_lens, (int)a.num_seqs, s_cu, s_warp, &s_bad);
+    const long long total_tokens = s_cu[a.num_seqs];
+    if (blockIdx.x == 0 && blockIdx.y == 0) {
+        for (int q = threadIdx.x; q <= a.num_seqs; q += kThreads) a.cu_seqlens[q] = s_cu[q];
+        if (threadIdx.x == 0) {
+            if (s_bad) record_error(a.err, kShapeMismatch, -1);
+            else if (total_tokens != a.num_tokens) record_error(a.err, kShapeMismatch, total_tokens);
         }
-        const long long pos = (long long)__ldg(ctx + lo) + (t - s_cu[lo]);
-        const long long lb = pos / block_size;
-        const long long off = pos - lb * block_size;
-        long long out = -1;
-        if (lb < table_stride) {
-            const long long blk = __ldg(tables + (long long)lo * table_stride + lb);
-            if (blk >= 0 && blk < num_blocks) out = blk * block_size + off;
-            else record_error(err, kInvalidBlock, t);
-        } else {
-            record_error(err, kSlotOutOfRange, t);
+    }
+    if (s_bad || total_tokens != a.num_tokens) return;
+
+    const long long entry_bytes = (long long)nvec * sizeof(V);
+    const long long pool_layer = a.slots_per_layer * entry_bytes;
+    const int l0 = blockIdx.y * layers_per_chunk;
+    const int l1 = min((int)a.num_layers, l0 + layers_per_chunk);
+    const long long src_tok = a.src_token_stride_bytes, src_layer = a.src_layer_stride_bytes;
+    const char *kbase = static_cast<const char *>(a.k);
+    const char *vbase = static_cast<const char *>(a.v);
+    char *kp = static_cast<char *>(a.k_pool) + a.first_layer * pool_layer;
+    char *vp = static_cast<char *>(a.v_pool) + a.first_layer * pool_layer;
+    const long long total = a.num_tokens * nvec;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x; it < total; it += stride) {
+        const long long t = it / nvec;
+        const int vec = (int)(it - t * nvec);
+        const bool lead = vec == 0 && blockIdx.y == 0;
+        const long long s = slot_of_token(t, s_cu, (int)a.num_seqs, a.ctx_lens, a.tables,
+                                          a.table_stride, a.block_size, a.num_blocks, a.err, lead);
+        if (lead && a.slots_out) a.slots_out[t] = s;
+        if (s < 0) continue;
+        const long long col = (long long)vec * sizeof(V);
+        const char *ks = kbase + t * src_tok + l0 * src_layer + col;
+        const char *vs = vbase + t * src_tok + l0 * src_layer + col;
+        char *kd = kp + l0 * pool_layer + s * entry_bytes + col;
+        char *vd = vp + l0 * pool_layer + s * entry_bytes + col;
+        int l = l0;
+        for (; l + UNROLL <= l1; l += UNROLL) {
+            V kr[UNROLL], vr[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                kr[u] = __ldcs(reinterpret_cast<const V *>(ks + u * src_layer));
+                vr[u] = __ldcs(reinterpret_cast<const V *>(vs + u * src_layer));
+            }
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                __stcs(reinterpret_cast<V *>(kd + u * pool_layer), kr[u]);
+                __stcs(reinterpret_cast<V *>(vd + u * pool_layer), vr[u]);
+            }
+            ks += UNROLL * src_layer;
+            vs += UNROLL * src_layer;
+            kd += UNROLL * pool_layer;
+            vd += UNROLL * pool_layer;
         }
-        slots[t] = out;
+        for (; l < l1; ++l) {
+            const V kr = __ldcs(reinterpret_cast<const V *>(ks));
+            const V vr = __ldcs(reinterpret_cast<const V *>(vs));
+            __stcs(reinterpret_cast<V *>(kd), kr);
+            __stcs(reinterpret_cast<V *>(vd), vr);
+            ks += src_layer;
+            vs += src_layer;
+            kd += pool_layer;
+            vd += pool_layer;
+        }
     }
 }
 
@@ -661,6 +760,43 @@ cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t 
         case DType::F16: return digest_rows_s<__half>(a, sms, st);
     }
     return cudaErrorInvalidValue;
+}
+
+namespace {
+template <typename V>
+cudaError_t resolve_cache_v(const ResolveCacheLaunch &a, long long entry_bytes, int sms,
+                            cudaStream_t st) {
+    const int nvec = (int)(entry_bytes / (long long)sizeof(V));
+    const long long items = a.num_tokens * nvec;
+    const long long want = (long long)sms * 2048 * 2;
+    long long chunks = std::min<long long>(a.num_layers, std::max<long long>(1, want / std::max<long long>(items, 1)));
+    const int lpc = (int)((a.num_layers + chunks - 1) / chunks);
+    chunks = (a.num_layers + lpc - 1) / lpc;
+    long long bx = std::min<long long>((items + kThreads - 1) / kThreads, (long long)sms * 256);
+    dim3 grid((unsigned)std::max<long long>(bx, 1), (unsigned)chunks);
+    const size_t smem = (size_t)(a.num_seqs + 1) * sizeof(int);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(resolve_cache_kernel<V, 4>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    resolve_cache_kernel<V, 4><<<grid, kThreads, smem, st>>>(a, nvec, lpc);
+    return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_resolve_cache(const ResolveCacheLaunch &a, int sms, cudaStream_t st) {
+    const long long entry_bytes = a.entry_bytes;
+    if (a.num_layers <= 0 || entry_bytes <= 0) return cudaSuccess;
+    const int vb = pick_vector_bytes(2, {entry_bytes, a.src_token_stride_bytes,
+                                         a.num_layers > 1 ? a.src_layer_stride_bytes : 0},
+                                     {a.k, a.v});
+    switch (vb) {
+        case 16: return resolve_cache_v<uint4>(a, entry_bytes, sms, st);
+        case 8: return resolve_cache_v<uint2>(a, entry_bytes, sms, st);
+        case 4: return resolve_cache_v<unsigned int>(a, entry_bytes, sms, st);
+        default: return resolve_cache_v<unsigned short>(a, entry_bytes, sms, st);
+    }
 }
 
 }  // namespace pkv

@@ -62,6 +62,8 @@ _PROTOS = {
     "pkv_copy_blocks_dev": (_I, [_P, _P, _I64, _P]),
     "pkv_zero_blocks_dev": (_I, [_P, _P, _I64, _P]),
     "pkv_resolve_slots_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P]),
+    "pkv_resolve_and_cache_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P, _P,
+                                       _I64, _I64, _I, _P]),
     "pkv_digest": (_I, [_P, C.POINTER(_U64), C.POINTER(_U64), _P]),
     "pkv_resolve_and_cache_noalloc": (_I, [C.POINTER(Config), _I, _I, _I, _P, _P, _P, _I64, _P, _P,
                                            _I64, _I64, _P, _I64, _P, _P, _I64, _I64, _I, _P, _P]),

@@ -222,6 +222,23 @@ class B200Backend:
                                          _ptr(new_lens), s, num_tokens, _ptr(cu_out),
                                          _ptr(slots_out), _stream_ptr(stream)))
 
+    def resolve_and_cache(self, block_tables, ctx_lens, new_lens, num_tokens: int, cu_out, k, v,
+                          layer: int | None = None, slots_out=None, stream=None) -> None:
+        """Fused slot resolution + reshape_and_cache (one launch); k, v as in
+        reshape_and_cache, slots_out optional."""
+        s = ctx_lens.shape[0]
+        stride = block_tables.shape[1] if block_tables.dim() == 2 else 0
+        tag = _torch_tag(k)
+        _same_layout(k, v)
+        if layer is None:
+            tok_stride, layer_stride, lay = k.stride(1), k.stride(0), -1
+        else:
+            tok_stride, layer_stride, lay = k.stride(0), 0, layer
+        _check(lib.pkv_resolve_and_cache_dev(self._h, _ptr(block_tables), stride, _ptr(ctx_lens),
+                                             _ptr(new_lens), s, num_tokens, _ptr(cu_out),
+                                             _ptr(slots_out), lay, _ptr(k), _ptr(v), tok_stride,
+                                             layer_stride, tag, _stream_ptr(stream)))
+
     def digest(self, stream=None) -> tuple[int, int]:
         k, v = C.c_uint64(), C.c_uint64()
         _check(lib.pkv_digest(self._h, C.byref(k), C.byref(v), _stream_ptr(stream)))

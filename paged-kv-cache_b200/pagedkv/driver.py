@@ -5,8 +5,9 @@ contract requires (crates/paged-kv-core/src/scheduler.rs:57-63):
 
 1. copy_blocks of the step's copy-on-write pairs (in dependency waves, so
    pairs that chain within the step keep their sequential meaning),
-2. slot resolution for the sequences given as block tables,
-3. one all-layer reshape_and_cache for every new token,
+2.+3. slot resolution for the sequences given as block tables fused with
+   their all-layer reshape_and_cache (one launch), then one all-layer
+   reshape_and_cache for the tokens whose slots the host supplied,
 4. zero_blocks of the blocks freed this step.
 
 Step metadata travels host -> device through reused pinned buffers; nothing
@@ -61,6 +62,12 @@ class _Staging:
         return out
 
 
+def _pool_dtype_matches(backend: B200Backend, t) -> bool:
+    import torch
+
+    return {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}.get(t.dtype) == backend.dtype_tag
+
+
 def copy_waves(copies: np.ndarray):
     """Orders a step's copy pairs into waves that may each run fully in
     parallel and, applied one after another, give the result of applying
@@ -99,7 +106,7 @@ class DeviceStepper:
     """Runs StepPlans on `backend`. With timing=True each step also records
     CUDA events around its four phases; ``phase_ms()`` sums them."""
 
-    PHASES = ("copy_blocks", "resolve_slots", "reshape_and_cache", "zero_blocks")
+    PHASES = ("copy_blocks", "resolve_and_cache", "reshape_and_cache", "zero_blocks")
 
     def __init__(self, backend: B200Backend, stream=None, timing: bool = False):
         import torch
@@ -165,7 +172,17 @@ class DeviceStepper:
             b.copy_blocks_dev(d_copies[2 * start:], count=count, stream=st)
             n += 1
         self._mark(marks)
-        if s:
+        rows = k.shape[1]
+        fused = s and tr <= rows and k.dtype == v.dtype and _pool_dtype_matches(b, k)
+        if fused:
+            # Slots resolved inline by the scatter itself; they are also
+            # published into self.slots for later readers of the cache.
+            b.resolve_and_cache(d_tables.view(torch.int32)[: tables.size].view(tables.shape),
+                                d_ctx.view(torch.int32)[:s], d_new.view(torch.int32)[:s], tr,
+                                self.cu, k[:, :tr], v[:, :tr], slots_out=self.slots[:tr],
+                                stream=st)
+            n += 1
+        elif s:
             b.resolve_slots(d_tables.view(torch.int32)[: tables.size].view(tables.shape),
                             d_ctx.view(torch.int32)[:s], d_new.view(torch.int32)[:s], tr,
                             self.cu, self.slots[:max(tr, 1)], stream=st)
@@ -174,11 +191,15 @@ class DeviceStepper:
             with torch.cuda.stream(st):
                 self.slots[tr:t].copy_(d_direct[:d], non_blocking=True)
         self._mark(marks)
-        rows = k.shape[1]
-        for c0 in range(0, t, rows):
-            c = min(rows, t - c0)
-            b.reshape_and_cache(k[:, :c], v[:, :c], self.slots[c0:c0 + c], stream=st)
+        # Token i reads row i % rows: scatter in runs that do not wrap.
+        start = tr if fused else 0
+        while start < t:
+            r0 = start % rows
+            c = min(rows - r0, t - start)
+            b.reshape_and_cache(k[:, r0:r0 + c], v[:, r0:r0 + c], self.slots[start:start + c],
+                                stream=st)
             n += 1
+            start += c
         self._mark(marks)
         if len(zero):
             b.zero_blocks_dev(d_zero, count=len(zero), stream=st)

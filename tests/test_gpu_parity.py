@@ -531,3 +531,78 @@ def test_empty_device_calls_launch_nothing_and_succeed(cuda):
     assert cu.item() == 0 and b.device_error() is None
     pk, pv = b.planes()
     assert int(torch.count_nonzero(pk)) == 0 and int(torch.count_nonzero(pv)) == 0
+
+
+@pytest.mark.parametrize("case", ["prefill", "decode", "per_layer", "no_slot_output", "sharded"])
+def test_fused_resolve_and_cache_equals_resolve_then_reshape(cuda, case):
+    """pkv_resolve_and_cache_dev (slots resolved inside the scatter) gives the
+    pool, cu_seqlens and slot mapping of pkv_resolve_slots_dev followed by
+    pkv_reshape_and_cache_dev, and the oracle's pool."""
+    import torch
+
+    cfg = CacheConfig(4096, 16, 4, 32, 4, 2)
+    e = cfg.entry_elems()
+    st = Stream({"prefill": 1, "decode": 2, "per_layer": 3, "no_slot_output": 4, "sharded": 5}[case])
+    if case == "decode":
+        batch = decode_batch(seed=None, num_seqs=200, max_ctx=500, cfg=cfg)
+    else:
+        from pagedkv.workloads import prefill_chunk
+        batch = prefill_chunk(seed=int(st.integers(1, 0, 100)[0]), num_prompts=30, lo=16, hi=600,
+                              budget=5000, cfg=cfg)
+    t = batch.num_tokens
+    shards = 2 if case == "sharded" else 1
+    w = e // shards
+    kv = f32_to_bf16_bits(st.normal(2 * cfg.num_layers * t * e)).reshape(2, cfg.num_layers, t, e)
+    d_kv = torch.from_numpy(kv.view(np.int16)).view(torch.bfloat16).to(cuda)
+    tab = torch.from_numpy(batch.tables).to(cuda)
+    ctx = torch.from_numpy(batch.ctx).to(cuda)
+    new = torch.from_numpy(batch.new).to(cuda)
+    layer = 2 if case == "per_layer" else None
+    for r in range(shards):
+        ks, vs = d_kv[0, ..., r * w:(r + 1) * w], d_kv[1, ..., r * w:(r + 1) * w]
+        if layer is not None:
+            ks, vs = ks[layer], vs[layer]
+        ref = B200Backend(cfg, dtype="bf16", shard_rank=r, num_shards=shards)
+        cu_ref = torch.empty(len(batch.new) + 1, dtype=torch.int32, device=cuda)
+        sl_ref = torch.empty(t, dtype=torch.int64, device=cuda)
+        ref.resolve_slots(tab, ctx, new, t, cu_ref, sl_ref)
+        ref.reshape_and_cache(ks, vs, sl_ref, layer=layer)
+        fus = B200Backend(cfg, dtype="bf16", shard_rank=r, num_shards=shards)
+        cu = torch.full_like(cu_ref, -1)
+        sl = None if case == "no_slot_output" else torch.full_like(sl_ref, -9)
+        fus.resolve_and_cache(tab, ctx, new, t, cu, ks, vs, layer=layer, slots_out=sl)
+        torch.cuda.synchronize()
+        assert ref.device_error() is None and fus.device_error() is None
+        assert torch.equal(cu, cu_ref)
+        if sl is not None:
+            assert torch.equal(sl, sl_ref)
+        for a, b in zip(fus.planes(), ref.planes()):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    if shards == 1 and layer is None:
+        cpu = OracleBackend(cfg)
+        slots = batch.slot_mapping()
+        dsts = [(int(x) // 16, int(x) % 16) for x in slots]
+        for l in range(cfg.num_layers):
+            cpu.write_kv_batch(l, dsts, bf16_bits_to_f32(kv[0, l]).ravel(), bf16_bits_to_f32(kv[1, l]).ravel())
+        assert_pools_equal(fus, cpu)
+
+
+def test_fused_resolve_and_cache_flags_bad_tables_and_writes_nothing_for_them(cuda):
+    import torch
+
+    cfg = CacheConfig(64, 4, 1, 8, 2, 2)
+    b = B200Backend(cfg, dtype="bf16")
+    tables = torch.tensor([[0, 70]], dtype=torch.int32, device=cuda)  # 70 is outside the pool
+    ctx = torch.tensor([3], dtype=torch.int32, device=cuda)
+    new = torch.tensor([3], dtype=torch.int32, device=cuda)
+    k = torch.ones((2, 3, 8), dtype=torch.bfloat16, device=cuda)
+    cu = torch.zeros(2, dtype=torch.int32, device=cuda)
+    sl = torch.zeros(3, dtype=torch.int64, device=cuda)
+    b.resolve_and_cache(tables, ctx, new, 3, cu, k, k, slots_out=sl)
+    err = b.device_error()
+    assert err is not None and isinstance(err[0], InvalidBlock)
+    assert sl.tolist() == [3, -1, -1]
+    pk, _ = b.planes()
+    assert int(torch.count_nonzero(pk)) == 2 * 8  # token 0 in both layers only
+    with pytest.raises(Exception, match="dtype"):
+        b.resolve_and_cache(tables, ctx, new, 3, cu, k.float(), k.float())
