@@ -581,6 +581,20 @@ cudaError_t launch_copy_v(const ReshapeLaunch &a, long long entry_bytes, int lay
     return cudaGetLastError();
 }
 
+// Layers per grid.y chunk of a scatter launch. Layers are split only when
+// the (token, vector) items alone cannot fill one wave of resident CTAs, and
+// never below 4 layers per chunk, so every thread keeps 4 layers' K and V
+// loads in flight and the per-CTA set-up is paid for over several layers.
+int layers_per_chunk(long long items, long long num_layers, int sms, long long *chunks) {
+    const long long wave = (long long)sms * 4 * kThreads;
+    const long long needed = (wave + std::max<long long>(items, 1) - 1) / std::max<long long>(items, 1);
+    const long long cap = std::max<long long>(1, (num_layers + 3) / 4);
+    const long long c = std::min<long long>(std::max<long long>(needed, 1), cap);
+    const int lpc = (int)((num_layers + c - 1) / c);
+    *chunks = (num_layers + lpc - 1) / lpc;
+    return lpc;
+}
+
 // Largest power-of-two vector width (<= 16 bytes) dividing every byte offset.
 int pick_vector_bytes(long long elem_bytes, std::initializer_list<long long> byte_quantities,
                       std::initializer_list<const void *> ptrs) {
@@ -608,12 +622,9 @@ cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t st) {
     if (a.num_tokens <= 0 || a.num_layers <= 0 || a.entry_elems <= 0) return cudaSuccess;
     const int es = dtype_size(a.pool_dtype);
     const long long entry_bytes = a.entry_elems * es;
-    // Split layers into chunks (grid.y) only when tokens alone cannot fill the GPU.
     const long long items = a.num_tokens * std::max<long long>(1, entry_bytes / 16);
-    const long long want = (long long)sms * 2048 * 2;
-    long long chunks = std::min<long long>(a.num_layers, std::max<long long>(1, want / std::max<long long>(items, 1)));
-    const int lpc = (int)((a.num_layers + chunks - 1) / chunks);
-    chunks = (a.num_layers + lpc - 1) / lpc;
+    long long chunks;
+    const int lpc = layers_per_chunk(items, a.num_layers, sms, &chunks);
 
     if (a.src_dtype == a.pool_dtype) {
         const int vb = pick_vector_bytes(
@@ -768,10 +779,8 @@ cudaError_t resolve_cache_v(const ResolveCacheLaunch &a, long long entry_bytes, 
                             cudaStream_t st) {
     const int nvec = (int)(entry_bytes / (long long)sizeof(V));
     const long long items = a.num_tokens * nvec;
-    const long long want = (long long)sms * 2048 * 2;
-    long long chunks = std::min<long long>(a.num_layers, std::max<long long>(1, want / std::max<long long>(items, 1)));
-    const int lpc = (int)((a.num_layers + chunks - 1) / chunks);
-    chunks = (a.num_layers + lpc - 1) / lpc;
+    long long chunks;
+    const int lpc = layers_per_chunk(items, a.num_layers, sms, &chunks);
     long long bx = std::min<long long>((items + kThreads - 1) / kThreads, (long long)sms * 256);
     dim3 grid((unsigned)std::max<long long>(bx, 1), (unsigned)chunks);
     const size_t smem = (size_t)(a.num_seqs + 1) * sizeof(int);

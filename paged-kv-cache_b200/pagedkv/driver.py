@@ -23,16 +23,21 @@ from .traces import StepPlan
 
 
 class _Staging:
-    """A pinned host buffer and a device buffer of int64 words, grown on demand."""
+    """A ring of pinned host buffers and one device buffer of int64 words,
+    grown on demand. The host reuses a pinned buffer only once the copy out of
+    it has finished, `ring` steps later, so it can stage a step while the GPU
+    is still busy with the previous ones. The device buffer is rewritten in
+    stream order, after the kernels of earlier steps have read it."""
 
-    def __init__(self, dev):
+    def __init__(self, dev, ring: int = 4):
         import torch
 
         self.torch = torch
         self.dev = dev
-        self.host = torch.empty(0, dtype=torch.int64).pin_memory()
+        self.host = [torch.empty(0, dtype=torch.int64).pin_memory() for _ in range(ring)]
+        self.events = [None] * ring
+        self.turn = 0
         self.device = torch.empty(0, dtype=torch.int64, device=dev)
-        self.event = None
 
     def upload(self, arrays: list[np.ndarray], stream):
         """Copy the int arrays (as int64 words, each 8-byte aligned) to the device
@@ -40,21 +45,24 @@ class _Staging:
         torch = self.torch
         words = [(a.nbytes + 7) // 8 for a in arrays]
         total = max(sum(words), 1)
-        if self.event is not None:
-            self.event.synchronize()  # the previous step's copy out of `host` is done
-        if self.host.numel() < total:
-            self.host = torch.empty(2 * total, dtype=torch.int64).pin_memory()
+        i = self.turn % len(self.host)
+        self.turn += 1
+        if self.events[i] is not None:
+            self.events[i].synchronize()  # the copy out of this pinned buffer is done
+        if self.host[i].numel() < total:
+            self.host[i] = torch.empty(2 * total, dtype=torch.int64).pin_memory()
         if self.device.numel() < total:
             self.device = torch.empty(2 * total, dtype=torch.int64, device=self.dev)
-        hb = self.host.numpy().view(np.uint8)
+        hb = self.host[i].numpy().view(np.uint8)
         off = 0
         for a, w in zip(arrays, words):
             hb[off * 8: off * 8 + a.nbytes] = np.ascontiguousarray(a).view(np.uint8).ravel()
             off += w
         with torch.cuda.stream(stream):
-            self.device[:total].copy_(self.host[:total], non_blocking=True)
-            self.event = torch.cuda.Event()
-            self.event.record(stream)
+            self.device[:total].copy_(self.host[i][:total], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            self.events[i] = ev
         out, off = [], 0
         for w in words:
             out.append(self.device[off: off + w])
