@@ -39,6 +39,26 @@ class _Staging:
         self.turn = 0
         self.device = torch.empty(0, dtype=torch.int64, device=dev)
 
+    def upload_packed(self, packed: np.ndarray, stream):
+        """Copy one int64 buffer to the device on `stream`; returns its device view."""
+        torch = self.torch
+        total = packed.size
+        i = self.turn % len(self.host)
+        self.turn += 1
+        if self.events[i] is not None:
+            self.events[i].synchronize()  # the copy out of this pinned buffer is done
+        if self.host[i].numel() < total:
+            self.host[i] = torch.empty(2 * total, dtype=torch.int64).pin_memory()
+        if self.device.numel() < total:
+            self.device = torch.empty(2 * total, dtype=torch.int64, device=self.dev)
+        self.host[i].numpy()[:total] = packed
+        with torch.cuda.stream(stream):
+            self.device[:total].copy_(self.host[i][:total], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            self.events[i] = ev
+        return self.device[:total]
+
     def upload(self, arrays: list[np.ndarray], stream):
         """Copy the int arrays (as int64 words, each 8-byte aligned) to the device
         on `stream`; returns a device int64 view per array."""
@@ -89,6 +109,14 @@ def copy_waves(copies: np.ndarray):
     pair that writes its source, reads its destination or writes its
     destination. Self-copies are dropped. Returns (ordered pairs [P'][2],
     [(start, count)] per wave)."""
+    copies = np.asarray(copies, np.int64).reshape(-1, 2)
+    if len(copies) == 0:
+        return np.zeros((0, 2), np.int64), []
+    src, dst = copies[:, 0], copies[:, 1]
+    if (src != dst).all() and np.unique(dst).size == len(dst) and \
+            np.intersect1d(src, dst, assume_unique=False).size == 0:
+        # No pair writes a block another pair reads or writes: one wave.
+        return np.ascontiguousarray(copies), [(0, len(copies))]
     last_write: dict[int, int] = {}
     last_read: dict[int, int] = {}
     keep, wave = [], []
@@ -157,26 +185,26 @@ class DeviceStepper:
         if self.cu.numel() < s + 1:
             self.cu = torch.empty(max(2 * (s + 1), 1024), dtype=torch.int32, device=self.dev)
 
-    def apply(self, plan: StepPlan, k, v) -> int:
-        """Runs one step. k, v: device [L][R][entry] rows; token i of the step
-        reads row i % R (R >= the step's token count keeps every row distinct)."""
+    def prepare(self, plan: StepPlan) -> "Prepared":
+        """Host-side work of a step done ahead of time: copy waves and one
+        packed buffer of every array the device needs."""
+        return Prepared(plan)
+
+    def apply(self, plan, k, v) -> int:
+        """Runs one step (a StepPlan, or one made ready by prepare()). k, v:
+        device [L][R][entry] rows; token i of the step reads row i % R
+        (R >= the step's token count keeps every row distinct)."""
         torch = self.torch
+        p = plan if isinstance(plan, Prepared) else Prepared(plan)
         b, st = self.b, self.stream
-        tr, d = plan.resolved_tokens, len(plan.direct_slots)
-        t, s = tr + d, len(plan.new)
+        tr, d, t, s = p.tr, p.d, p.t, p.s
         self._ensure(t, s)
-        tables = np.ascontiguousarray(plan.tables, np.int32)
-        copies, waves = copy_waves(np.asarray(plan.copies, np.int64).reshape(-1, 2))
-        ctx = np.ascontiguousarray(plan.ctx, np.int32)
-        new = np.ascontiguousarray(plan.new, np.int32)
-        direct = np.ascontiguousarray(plan.direct_slots, np.int64)
-        zero = np.ascontiguousarray(plan.zero, np.int64)
-        d_copies, d_tables, d_ctx, d_new, d_direct, d_zero = self.stage.upload(
-            [copies, tables, ctx, new, direct, zero], st)
+        dev = self.stage.upload_packed(p.packed, st)
+        d_copies, d_tables, d_ctx, d_new, d_direct, d_zero = (dev[a:c] for a, c in p.spans)
         n = 0
         marks: list = []
         self._mark(marks)
-        for start, count in waves:
+        for start, count in p.waves:
             b.copy_blocks_dev(d_copies[2 * start:], count=count, stream=st)
             n += 1
         self._mark(marks)
@@ -185,38 +213,66 @@ class DeviceStepper:
         if fused:
             # Slots resolved inline by the scatter itself; they are also
             # published into self.slots for later readers of the cache.
-            b.resolve_and_cache(d_tables.view(torch.int32)[: tables.size].view(tables.shape),
+            b.resolve_and_cache(d_tables.view(torch.int32)[: p.table_elems].view(p.table_shape),
                                 d_ctx.view(torch.int32)[:s], d_new.view(torch.int32)[:s], tr,
                                 self.cu, k[:, :tr], v[:, :tr], slots_out=self.slots[:tr],
                                 stream=st)
             n += 1
         elif s:
-            b.resolve_slots(d_tables.view(torch.int32)[: tables.size].view(tables.shape),
+            b.resolve_slots(d_tables.view(torch.int32)[: p.table_elems].view(p.table_shape),
                             d_ctx.view(torch.int32)[:s], d_new.view(torch.int32)[:s], tr,
                             self.cu, self.slots[:max(tr, 1)], stream=st)
             n += 1
-        if d:
+        self._mark(marks)
+        # Token i reads row i % rows: scatter in runs that do not wrap. Tokens
+        # past the resolved ones take their slots straight from the uploaded
+        # list; after a separate resolution every slot is in self.slots.
+        start = tr if fused or not s else 0
+        if not fused and s and d:
             with torch.cuda.stream(st):
                 self.slots[tr:t].copy_(d_direct[:d], non_blocking=True)
-        self._mark(marks)
-        # Token i reads row i % rows: scatter in runs that do not wrap.
-        start = tr if fused else 0
         while start < t:
             r0 = start % rows
             c = min(rows - r0, t - start)
-            b.reshape_and_cache(k[:, r0:r0 + c], v[:, r0:r0 + c], self.slots[start:start + c],
-                                stream=st)
+            slots = self.slots[start:start + c] if start < tr or (s and not fused) else \
+                d_direct[start - tr:start - tr + c]
+            b.reshape_and_cache(k[:, r0:r0 + c], v[:, r0:r0 + c], slots, stream=st)
             n += 1
             start += c
         self._mark(marks)
-        if len(zero):
-            b.zero_blocks_dev(d_zero, count=len(zero), stream=st)
+        if p.nzero:
+            b.zero_blocks_dev(d_zero, count=p.nzero, stream=st)
             n += 1
         self._mark(marks)
         if self.timing:
             self.events.append(marks)
         self.launches += n
         return n
+
+
+class Prepared:
+    """A StepPlan with its host-side work done: copy waves computed and every
+    array packed, as 8-byte-aligned int64 words, into one buffer."""
+
+    def __init__(self, plan: StepPlan):
+        tables = np.ascontiguousarray(plan.tables, np.int32)
+        copies, self.waves = copy_waves(plan.copies)
+        parts = [copies, tables, np.ascontiguousarray(plan.ctx, np.int32),
+                 np.ascontiguousarray(plan.new, np.int32),
+                 np.ascontiguousarray(plan.direct_slots, np.int64),
+                 np.ascontiguousarray(plan.zero, np.int64)]
+        words = [(a.nbytes + 7) // 8 for a in parts]
+        self.packed = np.zeros(max(sum(words), 1), np.int64)
+        raw = self.packed.view(np.uint8)
+        self.spans, off = [], 0
+        for a, w in zip(parts, words):
+            raw[off * 8: off * 8 + a.nbytes] = a.view(np.uint8).ravel()
+            self.spans.append((off, off + w))
+            off += w
+        self.tr, self.d = plan.resolved_tokens, len(plan.direct_slots)
+        self.t, self.s = self.tr + self.d, len(plan.new)
+        self.table_shape, self.table_elems = tables.shape, tables.size
+        self.nzero = len(plan.zero)
 
 
 def apply_to_oracle(orc, plan: StepPlan, k: np.ndarray, v: np.ndarray, resolve) -> None:
