@@ -498,14 +498,16 @@ def wl_trace(run, kind: str) -> dict:
     args, world, dev, stream = run.args, run.world, run.dev, run.stream
     W, K = args.warmup, args.steps
     if kind == "cow":
-        cfg = CacheConfig(num_blocks=BLOCKS_PER_CHUNK, **GEOM)
-        plans = list(beam_cow_trace(cfg, groups=64, width=4, prefix=2048, steps=W + K,
+        small = args.profile_small  # 512-token prefixes over a 4,096-block pool, for ncu
+        prefix = 512 if small else 2048
+        cfg = CacheConfig(num_blocks=4096 if small else BLOCKS_PER_CHUNK, **GEOM)
+        plans = list(beam_cow_trace(cfg, groups=64, width=4, prefix=prefix, steps=W + K,
                                     zero_per_step=64, seed=0))
-        rows = 64 * 2048
-        workload = ("beam search: 64 prefixes of 2048 tokens forked to 4 beams; every step "
+        rows = 64 * prefix
+        workload = (f"beam search: 64 prefixes of {prefix} tokens forked to 4 beams; every step "
                     "re-forks 4 children per group from seeded parents and appends one token to "
                     "each (copy-on-write of the shared tail), frees the old beams, zeroes 64 freed "
-                    "blocks; Qwen2-7B KV geometry, 32,768-block pool")
+                    f"blocks; Qwen2-7B KV geometry, {cfg.num_blocks}-block pool")
     else:
         heads, hd, layers = 8, 128, 80
         per_gpu = 150e9
