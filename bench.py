@@ -440,7 +440,9 @@ def wl_table_batch(run, kind: str) -> dict:
     kname = ("reshape_copy_kernel (all layers)" if args.unfused else
              "resolve_cache_kernel (slot resolution fused with the all-layer reshape_and_cache)")
     out["roofline"] = roofline(kname, alg_bytes, kernel_ms,
-                               profile_traffic("reshape_prefill_ncu") if kind == "prefill" else None)
+                               profile_traffic("reshape_prefill_ncu" if args.unfused else
+                                               "resolve_cache_prefill_ncu")
+                               if kind == "prefill" else None)
     if args.unfused:
         out["resolve_slots_ms"] = resolve_ms
     out["gpu_launches"] = (2 if args.unfused else 1) * K
@@ -584,7 +586,8 @@ def wl_trace(run, kind: str) -> dict:
     }
     if kind == "cow":
         out["roofline"] = roofline("copy_blocks_kernel (256 pairs x 28 layers per step)",
-                                   copy_bytes / len(timed), phase["copy_blocks"] / len(timed))
+                                   copy_bytes / len(timed), phase["copy_blocks"] / len(timed),
+                                   profile_traffic("copy_blocks_cow_ncu"))
     else:
         out["roofline"] = roofline("resolve_cache_kernel + reshape_copy_kernel (token writes, all "
                                    "layers)", write_bytes / len(timed), write_ms / len(timed))
