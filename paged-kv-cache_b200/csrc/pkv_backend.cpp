@@ -23,6 +23,10 @@ Status error(int code, int64_t a, int64_t b, std::string msg) {
 }
 
 Status device_error(const std::string &what, cudaError_t e) {
+    // Reset the runtime's last-error state, so that a recoverable failure
+    // (an allocation that did not fit) is not reported again by the next
+    // launch's cudaGetLastError.
+    cudaGetLastError();
     return error(PKV_ERR_DEVICE, 0, 0, what + ": " + cudaGetErrorString(e));
 }
 

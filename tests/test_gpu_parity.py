@@ -606,3 +606,17 @@ def test_fused_resolve_and_cache_flags_bad_tables_and_writes_nothing_for_them(cu
     assert int(torch.count_nonzero(pk)) == 2 * 8  # token 0 in both layers only
     with pytest.raises(Exception, match="dtype"):
         b.resolve_and_cache(tables, ctx, new, 3, cu, k.float(), k.float())
+
+
+def test_a_pool_larger_than_hbm_fails_cleanly_and_leaves_the_device_usable(cuda):
+    """Failure at init (CudaBackend::new's alloc_zeros): a 2.7 TB pool is a
+    Device error, not a crash, and the next backend works normally."""
+    from pagedkv import Device
+
+    huge = CacheConfig(num_blocks=2**20, block_size=16, num_kv_heads=8, head_dim=128,
+                       num_layers=80, dtype_bytes=2)
+    with pytest.raises(Device, match="allocating"):
+        B200Backend(huge, dtype="bf16")
+    b = B200Backend(CacheConfig.tiny(8))
+    b.write_kv(1, (3, 2), entry(1.0, 8), entry(2.0, 8))
+    assert (b.read_entry(1, (3, 2))[0] == entry(1.0, 8)).all()

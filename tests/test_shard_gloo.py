@@ -84,3 +84,45 @@ def test_entry_slices_tile_the_entry():
         assert cols == list(range(512))
     with pytest.raises(ValueError):
         entry_slice(512, 0, 3)
+
+
+def _dying_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    """Rank 1 exits between steps, before the verification collective; rank 0
+    must learn it from the collective (an error within the process-group
+    timeout), not hang."""
+    sys.path[:0] = [str(ROOT / "paged-kv-cache_b200"), str(ROOT)]
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from pagedkv.shard import verify_over_group
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    dist.barrier()
+    if rank == 1:
+        os._exit(3)  # a rank that dies between steps
+    try:
+        verify_over_group((1, 2), (1, 2))
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001 -- any collective failure is the detection
+        outcome = "error: " + type(e).__name__
+    Path(out_dir, "rank0.txt").write_text(outcome)
+    os._exit(0)
+
+
+def test_a_rank_that_dies_is_detected_by_the_survivor(tmp_path):
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_dying_rank_main, args=(r, 2, 29533, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a surviving rank hung instead of failing"
+    assert procs[1].exitcode == 3
+    assert Path(tmp_path, "rank0.txt").read_text().startswith("error")
