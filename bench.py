@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="decode: launch instead of graph replay")
     p.add_argument("--unfused", action="store_true",
                    help="resolve slots and scatter in two launches instead of the fused kernel")
+    p.add_argument("--copy-engine", choices=["auto", "vector", "bulk"], default="auto",
+                   help="cow/churn: copy_blocks engine (pkv_set_copy_engine)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-ops", action="store_true")
@@ -528,6 +530,7 @@ def wl_trace(run, kind: str) -> dict:
                     f"prompts, all-layer reshape_and_cache (freed blocks are not zeroed: the "
                     f"reference marks zero_block a debugging aid)")
     backend = B200Backend(cfg, dtype="bf16", device=run.local, shard_rank=run.rank, num_shards=world)
+    backend.set_copy_engine(args.copy_engine)
     es, L = backend.shard_entry_elems, cfg.num_layers
     gen = torch.Generator(device=dev).manual_seed(2000 + run.rank)
     k = torch.randn((L, rows, es), generator=gen, device=dev, dtype=torch.bfloat16)
@@ -573,7 +576,7 @@ def wl_trace(run, kind: str) -> dict:
         "steps_timed": len(timed), "warmup_steps": W, "layers": L, "entry_elems_per_gpu": es,
         "pool_gib_per_gpu": round(backend.allocated_bytes() / 2**30, 2),
         "parallelism": f"kv-head shards x{world}", "tokens_written": tokens,
-        "copy_pairs": copies, "zeroed_blocks": zeros,
+        "copy_pairs": copies, "zeroed_blocks": zeros, "copy_engine": args.copy_engine,
         "l2": "copies and writes stream through far more than the 126 MB L2 over the trace",
     }, "synthetic (seeded host trace through the native BlockAllocator/BlockTable/Scheduler)")
     out["gb_per_s"] = (copy_bytes + write_bytes + zero_bytes) * world / (total / 1e3) / 1e9
@@ -585,8 +588,10 @@ def wl_trace(run, kind: str) -> dict:
         "zero_blocks": zero_bytes / (phase["zero_blocks"] / 1e3) / 1e9 if phase["zero_blocks"] else None,
     }
     if kind == "cow":
-        out["roofline"] = roofline("copy_blocks_kernel (256 pairs x 28 layers per step)",
+        kern = "copy_blocks_bulk_kernel" if args.copy_engine == "bulk" else "copy_blocks_kernel"
+        out["roofline"] = roofline(f"{kern} (256 pairs x 28 layers per step)",
                                    copy_bytes / len(timed), phase["copy_blocks"] / len(timed),
+                                   None if args.copy_engine == "bulk" else
                                    profile_traffic("copy_blocks_cow_ncu"))
     else:
         out["roofline"] = roofline("resolve_cache_kernel + reshape_copy_kernel (token writes, all "
@@ -677,6 +682,11 @@ def bench_ops(backend, cfg, dev, stream, reps: int = 10) -> dict:
     pairs = torch.from_numpy(np.stack([ids[:256], ids[256:512]], 1).astype(np.int64)).to(dev)
     timed(lambda: backend.copy_blocks_dev(pairs, stream=stream),
           256 * L * 2 * block_bytes * 2 + 256 * 16, "copy_blocks", {"pairs": 256, "layers": L})
+    backend.set_copy_engine("bulk")
+    timed(lambda: backend.copy_blocks_dev(pairs, stream=stream),
+          256 * L * 2 * block_bytes * 2 + 256 * 16, "copy_blocks_bulk",
+          {"pairs": 256, "layers": L, "engine": "cp.async.bulk global->shared->global"})
+    backend.set_copy_engine("auto")
     zero = torch.from_numpy(ids[512:576].astype(np.int64)).to(dev)
     timed(lambda: backend.zero_blocks_dev(zero, stream=stream),
           64 * L * 2 * block_bytes + 64 * 8, "zero_blocks", {"blocks": 64})

@@ -155,6 +155,25 @@ int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, cons
  * device memory. The pairs must not chain (no dst is another pair's src or
  * dst), which copy-on-write pairs never do; src == dst is a no-op. */
 int pkv_copy_blocks_dev(pkv_backend *b, const int64_t *pairs, int64_t count, void *stream);
+/* Engines that copy_blocks can run on (no counterpart in the reference, whose
+ * copy_blocks_kernel, kernels.cu:62-92, has one scalar form). Both give the
+ * same pool bytes.
+ *   PKV_COPY_VECTOR: every thread moves 16-byte vectors through registers.
+ *   PKV_COPY_BULK:   one thread per CTA drives the SM's bulk-copy (TMA)
+ *                    engine, global -> shared -> global, in runs of up to
+ *                    32 KiB; needs a block plane (block_size * entry bytes)
+ *                    that splits into 16-byte multiples of at most 32 KiB.
+ *   PKV_COPY_AUTO:   the engine that measured faster on B200 for the pool's
+ *                    geometry (the default). */
+typedef enum pkv_copy_engine {
+    PKV_COPY_AUTO = 0,
+    PKV_COPY_VECTOR = 1,
+    PKV_COPY_BULK = 2
+} pkv_copy_engine;
+/* Selects the engine of every later copy_blocks call on this backend (host
+ * and device entry points). Unknown engines, and PKV_COPY_BULK for a geometry
+ * it cannot take, are rejected with PKV_ERR_DEVICE and leave the engine as it was. */
+int pkv_set_copy_engine(pkv_backend *b, int engine);
 /* zero_block (kernels.cu:94-110), batched: blocks = [count] int64 in device memory. */
 int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, void *stream);
 /* Slot resolution (no device counterpart in the reference; host rule

@@ -442,7 +442,7 @@ Status B200Backend::launch_copy_pairs(const uint64_t *pairs, uint64_t count) {
         a.pairs = static_cast<const long long *>(d_stage_) + 2 * r.first;
         a.num_pairs = (long long)(r.second - r.first);
         a.err = d_err_;
-        if ((e = launch_copy_blocks(a, stream_)) != cudaSuccess) return device_error("copy_blocks", e);
+        if ((e = launch_copy(a, stream_)) != cudaSuccess) return device_error("copy_blocks", e);
     }
     return Status::Ok();
 }
@@ -577,7 +577,32 @@ Status B200Backend::copy_blocks_dev(const int64_t *pairs, int64_t count, cudaStr
     a.pairs = reinterpret_cast<const long long *>(pairs);
     a.num_pairs = count;
     a.err = d_err_;
-    return check("copy_blocks", launch_copy_blocks(a, st));
+    return check("copy_blocks", launch_copy(a, st));
+}
+
+cudaError_t B200Backend::launch_copy(const CopyLaunch &a, cudaStream_t st) const {
+    // AUTO takes the register path: on B200 both engines reach the copy peak
+    // for 16 KiB plane-blocks, and the vector kernel needs no shared memory.
+    if (copy_engine_ == PKV_COPY_BULK) return launch_copy_blocks_bulk(a, sms_, st);
+    return launch_copy_blocks(a, st);
+}
+
+Status B200Backend::set_copy_engine(int engine) {
+    if (engine != PKV_COPY_AUTO && engine != PKV_COPY_VECTOR && engine != PKV_COPY_BULK)
+        return error(PKV_ERR_DEVICE, 0, 0, "unknown copy engine " + std::to_string(engine));
+    if (engine == PKV_COPY_BULK) {
+        CopyLaunch a{};
+        a.k_pool = k_plane_;
+        a.v_pool = v_plane_;
+        a.block_bytes = (long long)block_bytes();
+        if (!bulk_copy_supported(a))
+            return error(PKV_ERR_DEVICE, 0, 0,
+                         "bulk copy engine needs block planes that split into 16-byte runs of "
+                         "at most 32 KiB; this pool has " +
+                             std::to_string(block_bytes()) + "-byte block planes");
+    }
+    copy_engine_ = engine;
+    return Status::Ok();
 }
 
 Status B200Backend::zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t st) {

@@ -61,6 +61,7 @@ class B200Backend {
                                  DType src, cudaStream_t s);
     Status copy_blocks_dev(const int64_t *pairs, int64_t count, cudaStream_t s);
     Status zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t s);
+    Status set_copy_engine(int engine);
     Status resolve_slots_dev(const int32_t *tables, int64_t table_stride, const int32_t *ctx,
                              const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
                              int32_t *cu, int64_t *slots, cudaStream_t s);
@@ -101,6 +102,7 @@ class B200Backend {
                           const void *v, DType host);
     Status launch_copy_pairs(const uint64_t *pairs, uint64_t count);
     Status launch_zero_ids(const uint64_t *blocks, uint64_t count);
+    cudaError_t launch_copy(const CopyLaunch &a, cudaStream_t st) const;
     Status check(const char *what, cudaError_t e) const;
 
     pkv_config cfg_{};
@@ -108,6 +110,7 @@ class B200Backend {
     int device_ = 0;
     int sms_ = 148;
     int shard_rank_ = 0;
+    int copy_engine_ = PKV_COPY_AUTO;
     int num_shards_ = 1;
     uint64_t shard_entry_ = 0;
     void *k_plane_ = nullptr;

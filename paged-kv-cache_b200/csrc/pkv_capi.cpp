@@ -180,6 +180,11 @@ int pkv_copy_blocks_dev(pkv_backend *b, const int64_t *pairs, int64_t count, voi
     return guarded([&] { return b->impl->copy_blocks_dev(pairs, count, as_stream(stream)); });
 }
 
+int pkv_set_copy_engine(pkv_backend *b, int engine) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->set_copy_engine(engine); });
+}
+
 int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, void *stream) {
     if (!b) return null_handle();
     return guarded([&] { return b->impl->zero_blocks_dev(blocks, count, as_stream(stream)); });

@@ -136,6 +136,10 @@ int num_sms(int device);
 
 cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_copy_blocks(const CopyLaunch &a, cudaStream_t s);
+// copy_blocks through the SM's bulk-copy engine (pkv_bulk_copy.cu); supported
+// when a block's plane splits into 16-byte-aligned runs of at most 32 KiB.
+bool bulk_copy_supported(const CopyLaunch &a);
+cudaError_t launch_copy_blocks_bulk(const CopyLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_zero_blocks(const ZeroLaunch &a, cudaStream_t s);
 cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_resolve_cache(const ResolveCacheLaunch &a, int sms, cudaStream_t s);

@@ -26,6 +26,9 @@ F32, BF16, F16 = 0, 1, 2
 DTYPE_TAGS = {"f32": F32, "bf16": BF16, "f16": F16}
 DTYPE_BYTES = {F32: 4, BF16: 2, F16: 2}
 
+# pkv_copy_engine
+COPY_AUTO, COPY_VECTOR, COPY_BULK = 0, 1, 2
+
 
 class Config(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in
@@ -61,6 +64,7 @@ _PROTOS = {
     "pkv_reshape_and_cache_dev": (_I, [_P, _I64, _P, _P, _I64, _I64, _P, _I64, _I, _P]),
     "pkv_copy_blocks_dev": (_I, [_P, _P, _I64, _P]),
     "pkv_zero_blocks_dev": (_I, [_P, _P, _I64, _P]),
+    "pkv_set_copy_engine": (_I, [_P, _I]),
     "pkv_resolve_slots_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P]),
     "pkv_resolve_and_cache_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P, _P,
                                        _I64, _I64, _I, _P]),

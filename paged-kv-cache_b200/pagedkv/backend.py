@@ -209,6 +209,11 @@ class B200Backend:
         n = pairs.shape[0] if count is None else count
         _check(lib.pkv_copy_blocks_dev(self._h, _ptr(pairs), n, _stream_ptr(stream)))
 
+    def set_copy_engine(self, engine: str) -> None:
+        """Engine of later copy_blocks calls: "auto", "vector" or "bulk" (pkv_set_copy_engine)."""
+        tag = {"auto": _lib.COPY_AUTO, "vector": _lib.COPY_VECTOR, "bulk": _lib.COPY_BULK}[engine]
+        _check(lib.pkv_set_copy_engine(self._h, tag))
+
     def zero_blocks_dev(self, blocks, count: int | None = None, stream=None) -> None:
         n = blocks.shape[0] if count is None else count
         _check(lib.pkv_zero_blocks_dev(self._h, _ptr(blocks), n, _stream_ptr(stream)))
