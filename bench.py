@@ -637,9 +637,25 @@ def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks
         one()
     barrier()
     dt = max_over_ranks(time.perf_counter() - t0)
+    h2d = int(L * (2 * T * es * 2 + T * 8))
+    # The link's own ceiling: plain pinned host -> device copies of one layer's K and V rows.
+    src = torch.from_numpy(hk[0])
+    if not src.is_pinned():
+        src = src.pin_memory()
+    dst = torch.empty(src.shape, dtype=src.dtype, device=k.device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for i in range(4):
+        if i == 1:
+            ev[0].record()
+        dst.copy_(src, non_blocking=True)
+        dst.copy_(src, non_blocking=True)
+    ev[1].record()
+    torch.cuda.synchronize()
+    link = 3 * 2 * src.numel() * src.element_size() / (ev[0].elapsed_time(ev[1]) / 1e3) / 1e9
+    step_gbs = h2d * steps / dt / 1e9
     return {"value": T * steps / dt, "unit": "tokens/s",
-            "h2d_bytes_per_step": int(L * (2 * T * es * 2 + T * 8)),
-            "d2h_bytes_per_step": 16, "steps": steps,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 16, "steps": steps,
+            "h2d_gb_per_s": step_gbs, "link_h2d_gb_per_s": link, "frac_of_link": step_gbs / link,
             "path": "pkv_write_kv_batch per layer, pinned bf16 host rows, + pkv_device_error"}
 
 

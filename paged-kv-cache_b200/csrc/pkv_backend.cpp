@@ -263,37 +263,65 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
     const size_t slot_bytes = round_up(count * sizeof(int64_t), kAlign);
     const size_t kv_bytes = round_up(count * row_bytes, kAlign);
     Status s = ensure_device_stage(slot_bytes + 2 * kv_bytes);
-    if (!s.ok()) return s;
-    if (!(s = ensure_host_stage(count * sizeof(int64_t))).ok()) return s;
+    if (s.ok()) s = ensure_host_stage(count * sizeof(int64_t));
+    if (!s.ok()) {
+        // A batch whose first destination is invalid writes nothing and needs
+        // no staging: report the validation error, as CpuBackend would.
+        Status first = validate(layer, dsts[0]);
+        return first.ok() ? s : first;
+    }
+    char *d = static_cast<char *>(d_stage_);
+    int64_t *d_slots = reinterpret_cast<int64_t *>(d);
+    char *d_k = d + slot_bytes;
+    char *d_v = d_k + kv_bytes;
+
+    // The K/V rows go to the device first, so that the copy engine moves them
+    // while the host validates the destinations and builds the slot list.
+    // Rows past a failing destination are copied too but never scattered.
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(d_k, k, count * row_bytes, cudaMemcpyHostToDevice, stream_)) ||
+        (e = cudaMemcpyAsync(d_v, v, count * row_bytes, cudaMemcpyHostToDevice, stream_)) ||
+        (e = cudaEventRecord(inputs_consumed_, stream_))) {
+        cudaStreamSynchronize(stream_);  // never return while a copy may still read the caller's rows
+        return device_error("staging K/V", e);
+    }
+    // The caller's slices are borrowed: return only once they have been read.
+    auto finish_with = [&](Status st) {
+        const cudaError_t w = cudaEventSynchronize(inputs_consumed_);
+        if (st.ok() && w != cudaSuccess) return device_error("staging K/V", w);
+        return st;
+    };
+
+    // Validation in CpuBackend's order (cpu.rs:55-70); the items before the
+    // first bad one are applied, as by the trait's default loop (backend.rs:70-72).
+    uint64_t valid = 0;
+    Status bad;
+    for (; valid < count; ++valid) {
+        bad = validate(layer, dsts[valid]);
+        if (!bad.ok()) break;
+    }
+    if (valid == 0) return finish_with(bad);
 
     // Combined slot index block*block_size + slot (crates/paged-kv-cuda/src/backend.rs:172-175).
     // Within one batch the last write to a slot wins, as in the sequential
     // default write_kv_batch; earlier duplicates become padding (-1).
     int64_t *hs = static_cast<int64_t *>(h_stage_);
-    for (uint64_t i = 0; i < count; ++i) hs[i] = (int64_t)(dsts[i].block * cfg_.block_size + dsts[i].slot);
-    if (count > 1) {
+    for (uint64_t i = 0; i < valid; ++i) hs[i] = (int64_t)(dsts[i].block * cfg_.block_size + dsts[i].slot);
+    if (valid > 1) {
         if (seen_.size() * 64 < slots_per_layer()) seen_.assign((slots_per_layer() + 63) / 64, 0);
-        for (uint64_t i = count; i-- > 0;) {
+        for (uint64_t i = valid; i-- > 0;) {
             const uint64_t x = (uint64_t)hs[i];
             uint64_t &w = seen_[x >> 6];
             const uint64_t bit = 1ull << (x & 63);
             if (w & bit) hs[i] = -1;
             else w |= bit;
         }
-        for (uint64_t i = 0; i < count; ++i)
+        for (uint64_t i = 0; i < valid; ++i)
             if (hs[i] >= 0) seen_[(uint64_t)hs[i] >> 6] = 0;
     }
-    char *d = static_cast<char *>(d_stage_);
-    int64_t *d_slots = reinterpret_cast<int64_t *>(d);
-    char *d_k = d + slot_bytes;
-    char *d_v = d_k + kv_bytes;
-    cudaError_t e;
-    if ((e = cudaMemcpyAsync(d_slots, hs, count * sizeof(int64_t), cudaMemcpyHostToDevice, stream_)) ||
-        (e = cudaEventRecord(h_stage_free_, stream_)) ||
-        (e = cudaMemcpyAsync(d_k, k, count * row_bytes, cudaMemcpyHostToDevice, stream_)) ||
-        (e = cudaMemcpyAsync(d_v, v, count * row_bytes, cudaMemcpyHostToDevice, stream_)) ||
-        (e = cudaEventRecord(inputs_consumed_, stream_)))
-        return device_error("staging K/V", e);
+    if ((e = cudaMemcpyAsync(d_slots, hs, valid * sizeof(int64_t), cudaMemcpyHostToDevice, stream_)) ||
+        (e = cudaEventRecord(h_stage_free_, stream_)))
+        return finish_with(device_error("staging slots", e));
 
     ReshapeLaunch a{};
     a.k = d_k;
@@ -307,15 +335,13 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
     a.slots_per_layer = (long long)slots_per_layer();
     a.entry_elems = (long long)shard_entry_;
     a.slots = reinterpret_cast<const long long *>(d_slots);
-    a.num_tokens = (long long)count;
+    a.num_tokens = (long long)valid;
     a.src_dtype = host;
     a.pool_dtype = dtype_;
     a.err = d_err_;
-    if ((e = launch_reshape(a, sms_, stream_)) != cudaSuccess) return device_error("reshape_and_cache", e);
-    // The caller's slices are borrowed: return only once they have been read.
-    if ((e = cudaEventSynchronize(inputs_consumed_)) != cudaSuccess)
-        return device_error("staging K/V", e);
-    return Status::Ok();
+    if ((e = launch_reshape(a, sms_, stream_)) != cudaSuccess)
+        return finish_with(device_error("reshape_and_cache", e));
+    return finish_with(bad);
 }
 
 // write_kv (cpu.rs:95-111): validate, then K length, then V length.
@@ -340,15 +366,7 @@ Status B200Backend::write_kv_batch(uint64_t layer, const pkv_slot *dsts, uint64_
         return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)expected, (int64_t)k_len, msg_shape(expected, k_len));
     if (v_len != expected)
         return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)expected, (int64_t)v_len, msg_shape(expected, v_len));
-    uint64_t valid = 0;
-    Status bad;
-    for (; valid < count; ++valid) {
-        bad = validate(layer, dsts[valid]);
-        if (!bad.ok()) break;
-    }
-    Status s = launch_scatter(layer, dsts, valid, k, v, host);
-    if (!s.ok()) return s;
-    return bad;
+    return launch_scatter(layer, dsts, count, k, v, host);
 }
 
 // read_kv (cpu.rs:113-129): only the requested entry crosses PCIe.
