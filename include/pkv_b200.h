@@ -50,8 +50,13 @@ typedef enum pkv_status {
 } pkv_status;
 
 /* Element types of the pool and of caller buffers. CacheConfig only carries
- * dtype_bytes (config.rs:19-20); the type tag tells bf16 from f16. */
-typedef enum pkv_dtype { PKV_F32 = 0, PKV_BF16 = 1, PKV_F16 = 2 } pkv_dtype;
+ * dtype_bytes (config.rs:19-20); the type tag tells bf16 from f16.
+ * PKV_FP8_E4M3 (dtype_bytes 1) has no counterpart in the reference, whose
+ * CpuBackend is f32 only (cpu.rs:22-25): an fp8 pool stores OCP E4M3 codes,
+ * E4M3(x * (1/scale)) per (layer, kv head) -- see pkv_set_kv_scales. f32,
+ * bf16 and f16 rows are quantised on the way in and dequantised on the way
+ * out; E4M3 rows (raw codes) move unchanged and only to or from fp8 pools. */
+typedef enum pkv_dtype { PKV_F32 = 0, PKV_BF16 = 1, PKV_F16 = 2, PKV_FP8_E4M3 = 3 } pkv_dtype;
 
 /* CacheConfig (crates/paged-kv-core/src/config.rs:8-21), field for field. */
 typedef struct pkv_config {
@@ -146,7 +151,8 @@ int pkv_zero_blocks(pkv_backend *b, const uint64_t *blocks, uint64_t count);
  * [num_layers][num_tokens][entry] (layer pitch src_layer_stride elements) and
  * every layer is written in one launch. slot_mapping[t] = block*block_size +
  * slot; a negative slot skips the token (padding). src_dtype may differ from
- * the pool dtype (rounded to nearest even when narrowing). */
+ * the pool dtype (rounded to nearest even when narrowing; quantised with the
+ * pool's scales into an fp8 pool). */
 int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, const void *v,
                               int64_t src_token_stride, int64_t src_layer_stride,
                               const int64_t *slot_mapping, int64_t num_tokens, int src_dtype,
@@ -155,6 +161,18 @@ int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, cons
  * device memory. The pairs must not chain (no dst is another pair's src or
  * dst), which copy-on-write pairs never do; src == dst is a no-op. */
 int pkv_copy_blocks_dev(pkv_backend *b, const int64_t *pairs, int64_t count, void *stream);
+/* Scales of an fp8 (E4M3) pool; no counterpart in the reference. k_scales
+ * and v_scales are [num_layers][num_kv_heads] (count = num_layers *
+ * num_kv_heads, full heads even for a shard). Element x of layer l, kv head
+ * h is stored as E4M3(x * inv) with inv = 1.0f / scale[l][h] (f32 division),
+ * the product an f32 multiply, and the conversion rounding to nearest even
+ * and saturating at +-448; reads return code * scale. Every scale starts at
+ * 1.0. Each scale must be finite and positive with a finite reciprocal
+ * (else PKV_ERR_DEVICE); a wrong count is ShapeMismatch{expected, count};
+ * pools of other types reject the call. Applies to writes issued after it
+ * returns (it synchronises the backend's stream). */
+int pkv_set_kv_scales(pkv_backend *b, const float *k_scales, const float *v_scales,
+                      uint64_t count);
 /* Engines that copy_blocks can run on (no counterpart in the reference, whose
  * copy_blocks_kernel, kernels.cu:62-92, has one scalar form). Both give the
  * same pool bytes.
@@ -193,7 +211,8 @@ int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t t
  * arguments and results as pkv_resolve_slots_dev followed by
  * pkv_reshape_and_cache_dev(layer, k, v, ...); slot_mapping is an optional
  * output (NULL: not written) for kernels that read the cache afterwards.
- * src_dtype must equal the pool dtype. */
+ * src_dtype must equal the pool dtype, except that an fp8 pool also takes
+ * f32/bf16/f16 rows and quantises them in the same launch. */
 int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64_t table_stride,
                               const int32_t *ctx_lens, const int32_t *new_lens, int64_t num_seqs,
                               int64_t num_tokens, int32_t *cu_seqlens, int64_t *slot_mapping,

@@ -57,6 +57,9 @@ for name, res, args in [
     ("orc_resolve_slots", _I64, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),
     ("orc_digest_plane", _U64, [_P, _U64, C.c_uint32]),
     ("orc_digest_rows", _U64, [_P, _U64, _U64, _P, _U64, _U64, C.c_uint32]),
+    ("orc_set_fp8", C.c_int, [_P, _P, _P]),
+    ("orc_e4m3_from_f32_array", None, [_P, _U64, _P]),
+    ("orc_e4m3_to_f32", C.c_float, [C.c_uint8]),
 ]:
     f = getattr(_lib, name)
     f.restype = res
@@ -93,6 +96,14 @@ class OracleBackend:
             a, b = _I64(), _I64()
             _lib.orc_last_fields(self._h, C.byref(a), C.byref(b))
             raise RefError(rc, a.value, b.value)
+
+    def set_fp8(self, k_scales, v_scales) -> None:
+        """Makes this an fp8 (E4M3) pool with [num_layers][num_kv_heads] scales."""
+        self._k_scales = np.ascontiguousarray(k_scales, dtype=np.float32).ravel()
+        self._v_scales = np.ascontiguousarray(v_scales, dtype=np.float32).ravel()
+        n = self.cfg.num_layers * self.cfg.num_kv_heads
+        assert self._k_scales.size == n and self._v_scales.size == n
+        self._rc(_lib.orc_set_fp8(self._h, self._k_scales.ctypes.data, self._v_scales.ctypes.data))
 
     def write_kv(self, layer, dst, k, v):
         k, v = _f32(k), _f32(v)
@@ -181,3 +192,20 @@ def digest_rows(rows_f32: np.ndarray, slots: np.ndarray, layer: int, slots_per_l
 def digest_plane(plane_f32: np.ndarray, plane_id: int) -> int:
     p = np.ascontiguousarray(plane_f32, dtype=np.float32)
     return int(_lib.orc_digest_plane(p.ctypes.data, p.size, plane_id))
+
+
+def e4m3_from_f32(x) -> np.ndarray:
+    """E4M3 codes (uint8) of f32 values: round to nearest even, saturating to
+    +-448 (pkv_oracle.c, orc_e4m3_from_f32)."""
+    a = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(a.shape, np.uint8)
+    _lib.orc_e4m3_from_f32_array(a.ctypes.data, a.size, out.ctypes.data)
+    return out
+
+
+_E4M3_TABLE = np.array([_lib.orc_e4m3_to_f32(i) for i in range(256)], dtype=np.float32)
+
+
+def e4m3_to_f32(q) -> np.ndarray:
+    """Exact f32 values of E4M3 codes."""
+    return _E4M3_TABLE[np.asarray(q, dtype=np.uint8)]

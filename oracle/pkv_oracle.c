@@ -16,7 +16,8 @@
  * hold is replayed against this file by tests/test_oracle_pins.py.
  *
  * Storage is f32 whatever dtype_bytes says, exactly like CpuBackend
- * (cpu.rs:22-25). Element index:
+ * (cpu.rs:22-25); an fp8 pool (orc_set_fp8, no counterpart in the reference)
+ * stores the widened E4M3 codes in the same f32 planes. Element index:
  *   ((((layer*num_blocks + block)*block_size + slot)*num_kv_heads + head)*head_dim) + d
  * (cpu.rs:13-21, cpu.rs:45-53).
  */
@@ -53,6 +54,9 @@ typedef struct orc_backend {
     orc_config cfg;
     float *k, *v;     /* cpu.rs:27-31 */
     int64_t err_a, err_b; /* the failing variant's two fields */
+    /* fp8 (E4M3) pools only: per (layer, kv head) scales and their f32
+     * reciprocals; NULL for the f32/bf16/f16 pools of the reference. */
+    float *k_scale, *v_scale, *k_inv, *v_inv;
 } orc_backend;
 
 static uint64_t entry_elems(const orc_config *c) { return c->num_kv_heads * c->head_dim; } /* config.rs:50-52 */
@@ -86,7 +90,124 @@ void orc_free(orc_backend *b) {
     if (!b) return;
     free(b->k);
     free(b->v);
+    free(b->k_scale);
+    free(b->v_scale);
+    free(b->k_inv);
+    free(b->v_inv);
     free(b);
+}
+
+/*
+ * fp8 (E4M3) pools. The reference has none: CpuBackend stores f32 whatever
+ * dtype_bytes says (cpu.rs:22-25), and config.rs:19 only leaves room for
+ * 1-byte elements. This is the oracle of the device's quantising writes.
+ *
+ * Format: E4M3 of the OCP 8-bit floating point specification (OFP8, 2023):
+ * 1 sign bit, 4 exponent bits with bias 7, 3 mantissa bits; exponent 0 holds
+ * the subnormals m * 2^-9; S.1111.111 is NaN; there are no infinities and the
+ * largest finite magnitude is 448 (S.1111.110).
+ *
+ * Encoding of an f32 value: round to nearest, ties to even; magnitudes that
+ * would round past 448, and infinities, saturate to +-448 ("satfinite"); NaN
+ * encodes as S.1111.111 with the input's sign; -0.0 encodes as 0x80.
+ */
+uint8_t orc_e4m3_from_f32(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    const uint8_t sign = (uint8_t)((u >> 24) & 0x80);
+    const uint32_t a = u & 0x7fffffffu;
+    if (a > 0x7f800000u) return sign | 0x7f;          /* NaN */
+    if (a >= 0x43e00000u) return sign | 0x7e;         /* |x| >= 448: saturate */
+    const int e = (int)(a >> 23) - 127;               /* unbiased exponent */
+    if (e < -6) {
+        /* Below the smallest normal 2^-6: m * 2^-9, m = round(|x| * 512). The
+         * scaling by 512 is exact and y < 8, so y - floor(y) is exact too. */
+        float ax;
+        memcpy(&ax, &a, 4);
+        const float y = ax * 512.0f;
+        uint32_t m = (uint32_t)y;
+        const float frac = y - (float)m;
+        if (frac > 0.5f || (frac == 0.5f && (m & 1u))) ++m;
+        return sign | (uint8_t)m; /* m == 8 is 2^-6, the smallest normal: still right */
+    }
+    /* Normal: keep 3 of the 23 mantissa bits, round on the other 20. A carry
+     * out of the mantissa moves into the exponent field, which is again the
+     * correctly rounded value; below 448 it never reaches S.1111.111. */
+    const uint32_t mant = a & 0x7fffffu;
+    const uint32_t keep = mant >> 20, rest = mant & 0xfffffu, half = 0x80000u;
+    uint32_t q = ((uint32_t)(e + 7) << 3) | keep;
+    if (rest > half || (rest == half && (keep & 1u))) ++q;
+    return sign | (uint8_t)q;
+}
+
+/* Exact value of an E4M3 code as f32. */
+float orc_e4m3_to_f32(uint8_t q) {
+    const uint32_t sign = (uint32_t)(q & 0x80) << 24;
+    const uint32_t e = (q >> 3) & 0xfu, m = q & 7u;
+    uint32_t bits;
+    if (e == 15 && m == 7) {
+        bits = sign | 0x7fc00000u;
+    } else if (e == 0) {
+        float v = (float)m * (1.0f / 512.0f); /* exact */
+        memcpy(&bits, &v, 4);
+        bits |= sign;
+    } else {
+        bits = sign | ((e - 7 + 127) << 23) | (m << 20);
+    }
+    float out;
+    memcpy(&out, &bits, 4);
+    return out;
+}
+
+void orc_e4m3_from_f32_array(const float *x, uint64_t n, uint8_t *out) {
+    for (uint64_t i = 0; i < n; ++i) out[i] = orc_e4m3_from_f32(x[i]);
+}
+
+/* Makes this an fp8 pool: later writes store widen(E4M3(x * inv)) with
+ * inv = 1.0f / scale of the element's (layer, kv head), an f32 division and
+ * an f32 multiply, each rounded to nearest even; reads return the stored
+ * value times the scale. The planes hold the widened E4M3 values, so copies,
+ * zeroing and digests are unchanged. scales are [num_layers][num_kv_heads]. */
+int orc_set_fp8(orc_backend *b, const float *k_scales, const float *v_scales) {
+    const uint64_t n = b->cfg.num_layers * b->cfg.num_kv_heads;
+    float **dst[4] = {&b->k_scale, &b->v_scale, &b->k_inv, &b->v_inv};
+    for (int i = 0; i < 4; ++i) {
+        free(*dst[i]);
+        *dst[i] = (float *)malloc((n ? n : 1) * sizeof(float));
+        if (!*dst[i]) return fail(b, ORC_DEVICE, 0, 0);
+    }
+    for (uint64_t i = 0; i < n; ++i) {
+        b->k_scale[i] = k_scales[i];
+        b->v_scale[i] = v_scales[i];
+        b->k_inv[i] = 1.0f / k_scales[i];
+        b->v_inv[i] = 1.0f / v_scales[i];
+    }
+    return ORC_OK;
+}
+
+/* Stores one entry of `layer` at plane offset `off`, quantised when fp8. */
+static void store_entry(orc_backend *b, float *plane, const float *inv, uint64_t layer,
+                        uint64_t off, const float *src) {
+    const uint64_t n = b->cfg.num_kv_heads * b->cfg.head_dim;
+    if (!inv) {
+        memcpy(plane + off, src, n * sizeof(float));
+        return;
+    }
+    for (uint64_t i = 0; i < n; ++i) {
+        const float r = inv[layer * b->cfg.num_kv_heads + i / b->cfg.head_dim];
+        plane[off + i] = orc_e4m3_to_f32(orc_e4m3_from_f32(src[i] * r));
+    }
+}
+
+static void load_entry(orc_backend *b, const float *plane, const float *scale, uint64_t layer,
+                       uint64_t off, float *out) {
+    const uint64_t n = b->cfg.num_kv_heads * b->cfg.head_dim;
+    if (!scale) {
+        memcpy(out, plane + off, n * sizeof(float));
+        return;
+    }
+    for (uint64_t i = 0; i < n; ++i)
+        out[i] = plane[off + i] * scale[layer * b->cfg.num_kv_heads + i / b->cfg.head_dim];
 }
 
 float *orc_k_plane(orc_backend *b) { return b->k; }
@@ -138,8 +259,8 @@ int orc_write_kv(orc_backend *b, uint64_t layer, orc_slot dst, const float *k, u
     if ((rc = check_len(b, n, k_len))) return rc;
     if ((rc = check_len(b, n, v_len))) return rc;
     uint64_t off = slot_offset(b, layer, dst);
-    memcpy(b->k + off, k, n * sizeof(float));
-    memcpy(b->v + off, v, n * sizeof(float));
+    store_entry(b, b->k, b->k_inv, layer, off, k);
+    store_entry(b, b->v, b->v_inv, layer, off, v);
     return ORC_OK;
 }
 
@@ -168,8 +289,8 @@ int orc_read_kv(orc_backend *b, uint64_t layer, orc_slot src, float *k_out, uint
     if ((rc = check_len(b, n, k_len))) return rc;
     if ((rc = check_len(b, n, v_len))) return rc;
     uint64_t off = slot_offset(b, layer, src);
-    memcpy(k_out, b->k + off, n * sizeof(float));
-    memcpy(v_out, b->v + off, n * sizeof(float));
+    load_entry(b, b->k, b->k_scale, layer, off, k_out);
+    load_entry(b, b->v, b->v_scale, layer, off, v_out);
     return ORC_OK;
 }
 

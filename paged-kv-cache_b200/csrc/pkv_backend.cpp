@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <limits>
 #include <unordered_map>
@@ -61,8 +62,28 @@ std::string msg_layer(uint64_t l, uint64_t n) {
     return "invalid layer " + std::to_string(l) + ": model has " + std::to_string(n) + " layers";
 }
 
+// Exact f32 value of an E4M3 code (OCP OFP8 E4M3: bias 7, 3 mantissa bits,
+// exponent 0 holds m * 2^-9, S.1111.111 is NaN).
+float e4m3_to_f32(uint8_t q) {
+    const uint32_t sign = uint32_t(q & 0x80) << 24, e = (q >> 3) & 0xfu, m = q & 7u;
+    uint32_t bits;
+    if (e == 15 && m == 7) {
+        bits = sign | 0x7fc00000u;
+    } else if (e == 0) {
+        const float v = float(m) * (1.0f / 512.0f);
+        std::memcpy(&bits, &v, 4);
+        bits |= sign;
+    } else {
+        bits = sign | ((e + 120u) << 23) | (m << 20);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
 float host_to_f32(const void *p, uint64_t i, DType t) {
     switch (t) {
+        case DType::FP8_E4M3: return e4m3_to_f32(static_cast<const uint8_t *>(p)[i]);
         case DType::F32: return static_cast<const float *>(p)[i];
         case DType::BF16: {
             uint32_t bits = uint32_t(static_cast<const uint16_t *>(p)[i]) << 16;
@@ -80,6 +101,7 @@ void host_from_f32(void *p, uint64_t i, DType t, float f) {
         case DType::F32: static_cast<float *>(p)[i] = f; break;
         case DType::BF16: static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(f); break;
         case DType::F16: static_cast<__half *>(p)[i] = __float2half_rn(f); break;
+        case DType::FP8_E4M3: break;  // never a conversion target on the host
     }
 }
 
@@ -100,7 +122,7 @@ void host_convert(void *dst, DType dt, const void *src, DType st, uint64_t n) {
 
 Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int shard_rank,
                            int num_shards, std::unique_ptr<B200Backend> *out) {
-    if (static_cast<int>(dtype) < 0 || static_cast<int>(dtype) > 2)
+    if (static_cast<int>(dtype) < 0 || static_cast<int>(dtype) > 3)
         return error(PKV_ERR_DEVICE, 0, 0, "invalid config: unknown dtype tag");
     if (cfg.dtype_bytes != static_cast<uint64_t>(dtype_size(dtype)))
         return error(PKV_ERR_DEVICE, 0, 0,
@@ -166,6 +188,16 @@ Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int s
     b->d_digest_ = reinterpret_cast<unsigned long long *>(b->d_err_ + 1);
     if ((e = cudaMemsetAsync(b->d_err_, 0, sizeof(DevError), b->stream_)) != cudaSuccess)
         return device_error("cudaMemset", e);
+    if (dtype == DType::FP8_E4M3) {
+        // Per (layer, kv head) scales of K and V, 1.0 until pkv_set_kv_scales.
+        const size_t n = cfg.num_layers * cfg.num_kv_heads;
+        b->k_scale_.assign(n, 1.0f);
+        b->v_scale_.assign(n, 1.0f);
+        if ((e = cudaMalloc(&b->d_inv_, 2 * std::max<size_t>(n, 1) * sizeof(float))) != cudaSuccess)
+            return device_error("allocating fp8 scales", e);
+        Status st = b->upload_inv_scales();
+        if (!st.ok()) return st;
+    }
     if ((e = cudaStreamSynchronize(b->stream_)) != cudaSuccess) return device_error("init", e);
     *out = std::move(b);
     return Status::Ok();
@@ -177,6 +209,7 @@ B200Backend::~B200Backend() {
     if (k_plane_) cudaFree(k_plane_);
     if (v_plane_) cudaFree(v_plane_);
     if (d_err_) cudaFree(d_err_);
+    if (d_inv_) cudaFree(d_inv_);
     if (d_stage_) cudaFree(d_stage_);
     if (h_stage_) cudaFreeHost(h_stage_);
     if (h_stage_free_) cudaEventDestroy(h_stage_free_);
@@ -339,6 +372,7 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
     a.src_dtype = host;
     a.pool_dtype = dtype_;
     a.err = d_err_;
+    a.fp8 = fp8_scales();
     if ((e = launch_reshape(a, sms_, stream_)) != cudaSuccess)
         return finish_with(device_error("reshape_and_cache", e));
     return finish_with(bad);
@@ -347,6 +381,7 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
 // write_kv (cpu.rs:95-111): validate, then K length, then V length.
 Status B200Backend::write_kv(uint64_t layer, pkv_slot dst, const void *k, uint64_t k_len,
                              const void *v, uint64_t v_len, DType host) {
+    if (host == DType::FP8_E4M3 && dtype_ != DType::FP8_E4M3) return fp8_source_error();
     Status s = validate(layer, dst);
     if (!s.ok()) return s;
     if (k_len != shard_entry_)
@@ -361,6 +396,7 @@ Status B200Backend::write_kv(uint64_t layer, pkv_slot dst, const void *k, uint64
 Status B200Backend::write_kv_batch(uint64_t layer, const pkv_slot *dsts, uint64_t count,
                                    const void *k, uint64_t k_len, const void *v, uint64_t v_len,
                                    DType host) {
+    if (host == DType::FP8_E4M3 && dtype_ != DType::FP8_E4M3) return fp8_source_error();
     const uint64_t expected = count * shard_entry_;
     if (k_len != expected)
         return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)expected, (int64_t)k_len, msg_shape(expected, k_len));
@@ -372,6 +408,7 @@ Status B200Backend::write_kv_batch(uint64_t layer, const pkv_slot *dsts, uint64_
 // read_kv (cpu.rs:113-129): only the requested entry crosses PCIe.
 Status B200Backend::read_kv(uint64_t layer, pkv_slot src, void *k_out, uint64_t k_len, void *v_out,
                             uint64_t v_len, DType host) {
+    if (host == DType::FP8_E4M3 && dtype_ != DType::FP8_E4M3) return fp8_source_error();
     Status s = validate(layer, src);
     if (!s.ok()) return s;
     if (k_len != shard_entry_)
@@ -388,9 +425,67 @@ Status B200Backend::read_kv(uint64_t layer, pkv_slot src, void *k_out, uint64_t 
         (e = cudaMemcpyAsync(h + eb, static_cast<char *>(v_plane_) + off, eb, cudaMemcpyDeviceToHost, stream_)) ||
         (e = cudaEventRecord(h_stage_free_, stream_)) || (e = cudaStreamSynchronize(stream_)))
         return device_error("read_kv", e);
+    if (dtype_ == DType::FP8_E4M3 && host != DType::FP8_E4M3) {
+        // Dequantise: the widened code times its (layer, kv head) scale.
+        const uint64_t hd = cfg_.head_dim, base = layer * cfg_.num_kv_heads, off0 = elem_offset();
+        for (uint64_t i = 0; i < shard_entry_; ++i) {
+            const uint64_t sc = base + (off0 + i) / hd;
+            host_from_f32(k_out, i, host, e4m3_to_f32(static_cast<uint8_t>(h[i])) * k_scale_[sc]);
+            host_from_f32(v_out, i, host, e4m3_to_f32(static_cast<uint8_t>(h[eb + i])) * v_scale_[sc]);
+        }
+        return Status::Ok();
+    }
     host_convert(k_out, host, h, dtype_, shard_entry_);
     host_convert(v_out, host, h + eb, dtype_, shard_entry_);
     return Status::Ok();
+}
+
+Fp8Scales B200Backend::fp8_scales() const {
+    Fp8Scales f;
+    if (dtype_ != DType::FP8_E4M3) return f;
+    const long long n = (long long)(cfg_.num_layers * cfg_.num_kv_heads);
+    f.k_inv = d_inv_;
+    f.v_inv = d_inv_ + std::max<long long>(n, 1);
+    f.heads = (long long)cfg_.num_kv_heads;
+    f.head_dim = (long long)cfg_.head_dim;
+    f.elem_offset = (long long)elem_offset();
+    return f;
+}
+
+Status B200Backend::fp8_source_error() const {
+    return error(PKV_ERR_DEVICE, 0, 0, "E4M3 rows can only be written to (or read from) an fp8 pool");
+}
+
+Status B200Backend::upload_inv_scales() {
+    const size_t n = k_scale_.size(), stride = std::max<size_t>(n, 1);
+    std::vector<float> inv(2 * stride, 1.0f);
+    for (size_t i = 0; i < n; ++i) {
+        inv[i] = 1.0f / k_scale_[i];  // IEEE f32 division, rounded to nearest even
+        inv[stride + i] = 1.0f / v_scale_[i];
+    }
+    DeviceGuard g(device_);
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(d_inv_, inv.data(), inv.size() * sizeof(float), cudaMemcpyHostToDevice,
+                             stream_)) != cudaSuccess ||
+        (e = cudaStreamSynchronize(stream_)) != cudaSuccess)
+        return device_error("uploading fp8 scales", e);
+    return Status::Ok();
+}
+
+Status B200Backend::set_kv_scales(const float *k_scales, const float *v_scales, uint64_t count) {
+    if (dtype_ != DType::FP8_E4M3)
+        return error(PKV_ERR_DEVICE, 0, 0, "kv scales apply to fp8 (E4M3) pools only");
+    const uint64_t n = cfg_.num_layers * cfg_.num_kv_heads;
+    if (count != n) return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)n, (int64_t)count, msg_shape(n, count));
+    if (n > 0 && (!k_scales || !v_scales)) return error(PKV_ERR_DEVICE, 0, 0, "null scale array");
+    for (uint64_t i = 0; i < n; ++i)
+        for (float x : {k_scales[i], v_scales[i]})
+            if (!(x > 0.0f) || !std::isfinite(x) || !std::isfinite(1.0f / x))
+                return error(PKV_ERR_DEVICE, (int64_t)i, 0,
+                             "kv scale " + std::to_string(i) + " must be finite and positive, with a finite reciprocal");
+    k_scale_.assign(k_scales, k_scales + n);
+    v_scale_.assign(v_scales, v_scales + n);
+    return upload_inv_scales();
 }
 
 // ---------------------------------------------------------------------------
@@ -550,8 +645,9 @@ Status B200Backend::reshape_and_cache_dev(int64_t layer, const void *k, const vo
         return error(PKV_ERR_SHAPE_MISMATCH, 0, num_tokens, "negative token count");
     if (num_tokens == 0) return Status::Ok();
     if (!k || !v || !slots) return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
-    if (static_cast<int>(src) < 0 || static_cast<int>(src) > 2)
+    if (static_cast<int>(src) < 0 || static_cast<int>(src) > 3)
         return error(PKV_ERR_DEVICE, 0, 0, "unknown source dtype tag");
+    if (src == DType::FP8_E4M3 && dtype_ != DType::FP8_E4M3) return fp8_source_error();
     if (tok_stride <= 0) tok_stride = (int64_t)shard_entry_;
     if ((uint64_t)tok_stride < shard_entry_)
         return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)shard_entry_, tok_stride,
@@ -578,6 +674,7 @@ Status B200Backend::reshape_and_cache_dev(int64_t layer, const void *k, const vo
     a.src_dtype = src;
     a.pool_dtype = dtype_;
     a.err = d_err_;
+    a.fp8 = fp8_scales();
     return check("reshape_and_cache", launch_reshape(a, sms_, st));
 }
 
@@ -694,10 +791,14 @@ Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_s
     if (num_tokens > std::numeric_limits<int32_t>::max())
         return error(PKV_ERR_SHAPE_MISMATCH, std::numeric_limits<int32_t>::max(), num_tokens,
                      "too many tokens for int32 cu_seqlens");
-    if (src != dtype_)
+    const bool quantise = dtype_ == DType::FP8_E4M3 && src != DType::FP8_E4M3;
+    if (static_cast<int>(src) < 0 || static_cast<int>(src) > 3)
+        return error(PKV_ERR_DEVICE, 0, 0, "unknown source dtype tag");
+    if (src != dtype_ && !quantise)
         return error(PKV_ERR_DEVICE, 0, 0,
-                     "the fused path moves bytes: source dtype must equal the pool dtype "
-                     "(use pkv_resolve_slots_dev + pkv_reshape_and_cache_dev to convert)");
+                     "the fused path moves bytes, or quantises into an fp8 pool: source dtype "
+                     "must equal the pool dtype (use pkv_resolve_slots_dev + "
+                     "pkv_reshape_and_cache_dev to convert)");
     if (!cu || (num_seqs > 0 && (!ctx || !new_lens)) ||
         (num_tokens > 0 && (!tables || !k || !v)))
         return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
@@ -711,7 +812,7 @@ Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_s
         return error(PKV_ERR_SHAPE_MISMATCH, tok_stride * num_tokens, layer_stride,
                      "layer stride shorter than a layer's rows");
     DeviceGuard g(device_);
-    const int es = dtype_size(dtype_);
+    const int es = dtype_size(src);
     ResolveCacheLaunch a{};
     a.tables = tables;
     a.table_stride = table_stride;
@@ -734,6 +835,13 @@ Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_s
     a.slots_per_layer = (long long)slots_per_layer();
     a.entry_bytes = (long long)entry_bytes();
     a.err = d_err_;
+    if (quantise) {
+        a.src_dtype = src;
+        a.pool_dtype = dtype_;
+        a.entry_elems = (long long)shard_entry_;
+        a.fp8 = fp8_scales();
+        return check("resolve_and_cache", launch_resolve_cache_fp8(a, sms_, st));
+    }
     return check("resolve_and_cache", launch_resolve_cache(a, sms_, st));
 }
 
@@ -794,6 +902,7 @@ Status B200Backend::digest_rows(int64_t layer, const void *k, const void *v, int
     a.src_dtype = src;
     a.pool_dtype = dtype_;
     a.out = d_digest_;
+    a.fp8 = fp8_scales();
     if ((e = launch_digest_rows(a, sms_, st)) != cudaSuccess) return device_error("digest_rows", e);
     if ((e = cudaMemcpyAsync(host, d_digest_, sizeof(host), cudaMemcpyDeviceToHost, st)) ||
         (e = cudaStreamSynchronize(st)))

@@ -62,6 +62,7 @@ class B200Backend {
     Status copy_blocks_dev(const int64_t *pairs, int64_t count, cudaStream_t s);
     Status zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t s);
     Status set_copy_engine(int engine);
+    Status set_kv_scales(const float *k_scales, const float *v_scales, uint64_t count);
     Status resolve_slots_dev(const int32_t *tables, int64_t table_stride, const int32_t *ctx,
                              const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
                              int32_t *cu, int64_t *slots, cudaStream_t s);
@@ -103,6 +104,9 @@ class B200Backend {
     Status launch_copy_pairs(const uint64_t *pairs, uint64_t count);
     Status launch_zero_ids(const uint64_t *blocks, uint64_t count);
     cudaError_t launch_copy(const CopyLaunch &a, cudaStream_t st) const;
+    Fp8Scales fp8_scales() const;
+    Status fp8_source_error() const;
+    Status upload_inv_scales();
     Status check(const char *what, cudaError_t e) const;
 
     pkv_config cfg_{};
@@ -126,6 +130,10 @@ class B200Backend {
     cudaEvent_t h_stage_free_ = nullptr;  // last H2D out of h_stage_ has finished
     cudaEvent_t inputs_consumed_ = nullptr;
     std::vector<uint64_t> seen_;  // one bit per slot of a layer: duplicate detection
+    // fp8 pools: [num_layers][num_kv_heads] scales on the host, and their f32
+    // reciprocals on the device (K's, then V's).
+    std::vector<float> k_scale_, v_scale_;
+    float *d_inv_ = nullptr;
     std::string gpu_name_;
 };
 

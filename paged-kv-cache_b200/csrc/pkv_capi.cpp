@@ -30,7 +30,7 @@ namespace {
 
 int null_handle() { return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "null backend handle")); }
 
-bool valid_dtype(int t) { return t >= PKV_F32 && t <= PKV_F16; }
+bool valid_dtype(int t) { return t >= PKV_F32 && t <= PKV_FP8_E4M3; }
 
 int bad_dtype() { return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "unknown dtype tag")); }
 
@@ -178,6 +178,12 @@ int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, cons
 int pkv_copy_blocks_dev(pkv_backend *b, const int64_t *pairs, int64_t count, void *stream) {
     if (!b) return null_handle();
     return guarded([&] { return b->impl->copy_blocks_dev(pairs, count, as_stream(stream)); });
+}
+
+int pkv_set_kv_scales(pkv_backend *b, const float *k_scales, const float *v_scales,
+                      uint64_t count) {
+    if (!b) return null_handle();
+    return guarded([&] { return b->impl->set_kv_scales(k_scales, v_scales, count); });
 }
 
 int pkv_set_copy_engine(pkv_backend *b, int engine) {

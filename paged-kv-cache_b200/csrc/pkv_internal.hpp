@@ -7,9 +7,26 @@
 namespace pkv {
 
 // Element type tags; values match pkv_dtype in include/pkv_b200.h.
-enum class DType : int { F32 = 0, BF16 = 1, F16 = 2 };
+enum class DType : int { F32 = 0, BF16 = 1, F16 = 2, FP8_E4M3 = 3 };
 
-inline int dtype_size(DType t) { return t == DType::F32 ? 4 : 2; }
+inline int dtype_size(DType t) {
+    switch (t) {
+        case DType::F32: return 4;
+        case DType::FP8_E4M3: return 1;
+        default: return 2;
+    }
+}
+
+// Quantisation of an fp8 (E4M3) pool: element e of an entry held by this
+// backend belongs to kv head (elem_offset + e) / head_dim, and layer l of
+// head h stores E4M3(x * inv[l * heads + h]). Unused for other pool types.
+struct Fp8Scales {
+    const float *k_inv = nullptr;  // [num_layers][heads], device memory
+    const float *v_inv = nullptr;
+    long long heads = 0;
+    long long head_dim = 0;
+    long long elem_offset = 0;
+};
 
 // First bad index met by a device entry point. `code` is a pkv_status;
 // `index` is the token / pair / block index it was met at.
@@ -38,6 +55,7 @@ struct ReshapeLaunch {
     DType src_dtype;
     DType pool_dtype;
     DevError *err;
+    Fp8Scales fp8;  // pool_dtype == FP8_E4M3 with another src_dtype
 };
 
 // Batched block copy over every layer and both planes; pairs is [num_pairs][2].
@@ -109,8 +127,13 @@ struct ResolveCacheLaunch {
     long long first_layer;
     long long num_layers;
     long long slots_per_layer;
-    long long entry_bytes;
+    long long entry_bytes;  // pool bytes per entry
     DevError *err;
+    // Quantising form (fp8 pool, wider source): element types and scales.
+    DType src_dtype = DType::F32;
+    DType pool_dtype = DType::F32;
+    long long entry_elems = 0;
+    Fp8Scales fp8;
 };
 
 // Digest of rows as a scatter into an empty pool would store them.
@@ -130,6 +153,7 @@ struct DigestRowsLaunch {
     DType src_dtype;
     DType pool_dtype;
     unsigned long long *out;  // [2], accumulated
+    Fp8Scales fp8;
 };
 
 int num_sms(int device);
@@ -145,5 +169,12 @@ cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t s
 cudaError_t launch_resolve_cache(const ResolveCacheLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t s);
+
+// fp8 (E4M3) pools (pkv_fp8.cu): quantising scatter, fused slot resolution +
+// quantising scatter, and the digests of E4M3 planes and rows.
+cudaError_t launch_reshape_fp8(const ReshapeLaunch &a, int sms, cudaStream_t s);
+cudaError_t launch_resolve_cache_fp8(const ResolveCacheLaunch &a, int sms, cudaStream_t s);
+cudaError_t launch_digest_fp8(const DigestLaunch &a, int sms, cudaStream_t s);
+cudaError_t launch_digest_rows_fp8(const DigestRowsLaunch &a, int sms, cudaStream_t s);
 
 }  // namespace pkv

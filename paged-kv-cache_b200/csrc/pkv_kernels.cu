@@ -20,21 +20,11 @@
 #include <algorithm>
 #include <cstdint>
 
+#include "pkv_device.cuh"
 #include "pkv_internal.hpp"
 
 namespace pkv {
 namespace {
-
-constexpr int kThreads = 256;
-
-// pkv_status values recorded on the device.
-constexpr int kInvalidBlock = 2;
-constexpr int kSlotOutOfRange = 5;
-constexpr int kShapeMismatch = 6;
-
-__device__ __forceinline__ void record_error(DevError *e, int code, long long index) {
-    if (atomicCAS(&e->code, 0, code) == 0) e->index = index;
-}
 
 // ---- element conversion ---------------------------------------------------
 
@@ -262,83 +252,8 @@ zero_blocks_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_
 // contiguous segment per thread, then warp shuffles), so no CTA waits for
 // another; CTA 0 also publishes cu_seqlens. Each token then finds its
 // sequence by binary search over the prefix and applies
-// BlockTable::slot_for_position (block_table.rs:97-101).
-
-__device__ __forceinline__ int warp_inclusive_scan(int x) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    return x;
-}
-
-// Exclusive prefix of new_lens into s_cu[0..num_seqs] (one contiguous
-// segment per thread, then warp shuffles); sets *s_bad when a length or a
-// context is negative. Every thread of the CTA must call it.
-__device__ __forceinline__ void scan_lengths(const int *__restrict__ ctx,
-                                             const int *__restrict__ nnew, int num_seqs,
-                                             int *s_cu, int *s_warp, int *s_bad) {
-    const int tid = threadIdx.x;
-    if (tid == 0) *s_bad = 0;
-    __syncthreads();
-    const int seg = (num_seqs + kThreads - 1) / kThreads;
-    const int b0 = min(num_seqs, tid * seg);
-    const int b1 = min(num_seqs, b0 + seg);
-    int local = 0;
-    for (int q = b0; q < b1; ++q) {
-        const int n = __ldg(nnew + q);
-        if (n < 0 || __ldg(ctx + q) < 0) *s_bad = 1;
-        local += max(n, 0);
-    }
-    const int incl = warp_inclusive_scan(local);
-    if ((tid & 31) == 31) s_warp[tid >> 5] = incl;
-    __syncthreads();
-    if (tid < 32) {
-        const int w = tid < kThreads / 32 ? s_warp[tid] : 0;
-        const int wi = warp_inclusive_scan(w);
-        if (tid < kThreads / 32) s_warp[tid] = wi - w;
-    }
-    __syncthreads();
-    int run = s_warp[tid >> 5] + incl - local;
-    for (int q = b0; q < b1; ++q) {
-        s_cu[q] = run;
-        run += max(__ldg(nnew + q), 0);
-    }
-    if (b1 == num_seqs && b0 < b1) s_cu[num_seqs] = run;
-    if (num_seqs == 0 && tid == 0) s_cu[0] = 0;
-    __syncthreads();
-}
-
-// Combined slot of packed token t: its sequence by binary search over the
-// prefix, then BlockTable::slot_for_position. -1 (and an error record when
-// `report`) for a logical block past the table or a table entry outside the pool.
-__device__ __forceinline__ long long slot_of_token(long long t, const int *s_cu, int num_seqs,
-                                                   const int *__restrict__ ctx,
-                                                   const int *__restrict__ tables,
-                                                   long long table_stride, long long block_size,
-                                                   long long num_blocks, DevError *err, bool report) {
-    int lo = 0, hi = num_seqs - 1;
-    while (lo < hi) {  // last q with s_cu[q] <= t; that sequence has new_lens > 0
-        const int mid = (lo + hi + 1) >> 1;
-        if (s_cu[mid] <= t) lo = mid;
-        else hi = mid - 1;
-    }
-    const long long pos = (long long)__ldg(ctx + lo) + (t - s_cu[lo]);
-    const long long lb = pos / block_size;
-    const long long off = pos - lb * block_size;
-    if (lb >= table_stride) {
-        if (report) record_error(err, kSlotOutOfRange, t);
-        return -1;
-    }
-    const long long blk = __ldg(tables + (long long)lo * table_stride + lb);
-    if (blk < 0 || blk >= num_blocks) {
-        if (report) record_error(err, kInvalidBlock, t);
-        return -1;
-    }
-    return blk * block_size + off;
-}
+// BlockTable::slot_for_position (block_table.rs:97-101); the scan and the
+// slot rule live in pkv_device.cuh.
 
 __global__ void __launch_bounds__(kThreads)
 resolve_slots_kernel(const int *__restrict__ tables, long long table_stride,
@@ -448,13 +363,7 @@ resolve_cache_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
 }
 
 // ---- digest --------------------------------------------------------------------
-// splitmix64 finaliser (Steele, Lea & Flood, 2014) over (global index, bits).
-
-__device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    return z ^ (z >> 31);
-}
+// splitmix64 finaliser over (global index, bits): mix64 in pkv_device.cuh.
 
 __device__ __forceinline__ unsigned widen_bits(const float *p, long long i) { return __float_as_uint(p[i]); }
 __device__ __forceinline__ unsigned widen_bits(const __nv_bfloat16 *p, long long i) {
@@ -526,7 +435,6 @@ digest_rows_kernel(const S *__restrict__ k, const S *__restrict__ v, long long t
 
 // ---- helpers ---------------------------------------------------------------------
 
-inline bool aligned(const void *p, long long a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 template <typename S, typename D>
 cudaError_t launch_convert(const ReshapeLaunch &a, dim3 grid_chunks, int layers_per_chunk,
@@ -558,8 +466,8 @@ cudaError_t launch_convert_from(const ReshapeLaunch &a, dim3 g, int lpc, bool pe
         case DType::F32: return launch_convert<S, float>(a, g, lpc, per8, sms, st);
         case DType::BF16: return launch_convert<S, __nv_bfloat16>(a, g, lpc, per8, sms, st);
         case DType::F16: return launch_convert<S, __half>(a, g, lpc, per8, sms, st);
+        default: return cudaErrorInvalidValue;
     }
-    return cudaErrorInvalidValue;
 }
 
 template <typename V>
@@ -581,33 +489,6 @@ cudaError_t launch_copy_v(const ReshapeLaunch &a, long long entry_bytes, int lay
     return cudaGetLastError();
 }
 
-// Layers per grid.y chunk of a scatter launch. Layers are split only when
-// the (token, vector) items alone cannot fill one wave of resident CTAs, and
-// never below 4 layers per chunk, so every thread keeps 4 layers' K and V
-// loads in flight and the per-CTA set-up is paid for over several layers.
-int layers_per_chunk(long long items, long long num_layers, int sms, long long *chunks) {
-    const long long wave = (long long)sms * 4 * kThreads;
-    const long long needed = (wave + std::max<long long>(items, 1) - 1) / std::max<long long>(items, 1);
-    const long long cap = std::max<long long>(1, (num_layers + 3) / 4);
-    const long long c = std::min<long long>(std::max<long long>(needed, 1), cap);
-    const int lpc = (int)((num_layers + c - 1) / c);
-    *chunks = (num_layers + lpc - 1) / lpc;
-    return lpc;
-}
-
-// Largest power-of-two vector width (<= 16 bytes) dividing every byte offset.
-int pick_vector_bytes(long long elem_bytes, std::initializer_list<long long> byte_quantities,
-                      std::initializer_list<const void *> ptrs) {
-    int vb = 16;
-    while (vb > elem_bytes) {
-        bool ok = true;
-        for (long long q : byte_quantities) ok = ok && (q % vb == 0);
-        for (const void *p : ptrs) ok = ok && aligned(p, vb);
-        if (ok) break;
-        vb /= 2;
-    }
-    return vb;
-}
 
 }  // namespace
 
@@ -620,6 +501,10 @@ int num_sms(int device) {
 
 cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t st) {
     if (a.num_tokens <= 0 || a.num_layers <= 0 || a.entry_elems <= 0) return cudaSuccess;
+    if (a.pool_dtype == DType::FP8_E4M3 && a.src_dtype != DType::FP8_E4M3)
+        return launch_reshape_fp8(a, sms, st);  // quantising scatter (pkv_fp8.cu)
+    if (a.src_dtype == DType::FP8_E4M3 && a.pool_dtype != DType::FP8_E4M3)
+        return cudaErrorInvalidValue;  // E4M3 rows go only into E4M3 pools
     const int es = dtype_size(a.pool_dtype);
     const long long entry_bytes = a.entry_elems * es;
     const long long items = a.num_tokens * std::max<long long>(1, entry_bytes / 16);
@@ -646,8 +531,8 @@ cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t st) {
         case DType::F32: return launch_convert_from<float>(a, g, lpc, per8, sms, st);
         case DType::BF16: return launch_convert_from<__nv_bfloat16>(a, g, lpc, per8, sms, st);
         case DType::F16: return launch_convert_from<__half>(a, g, lpc, per8, sms, st);
+        default: return cudaErrorInvalidValue;
     }
-    return cudaErrorInvalidValue;
 }
 
 namespace {
@@ -717,6 +602,7 @@ cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t s
 cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t st) {
     const long long total = a.rows * a.entry_elems;
     if (total <= 0) return cudaSuccess;
+    if (a.pool_dtype == DType::FP8_E4M3) return launch_digest_fp8(a, sms, st);
     long long bx = std::min<long long>((total + kThreads - 1) / kThreads, (long long)sms * 16);
     dim3 grid((unsigned)std::max<long long>(bx, 1), 2);
     switch (a.pool_dtype) {
@@ -736,6 +622,7 @@ cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t st) {
                 static_cast<const __half *>(a.k_pool), static_cast<const __half *>(a.v_pool),
                 a.rows, a.entry_elems, a.full_entry, a.elem_offset, a.out);
             break;
+        default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
@@ -758,19 +645,20 @@ cudaError_t digest_rows_s(const DigestRowsLaunch &a, int sms, cudaStream_t st) {
         case DType::F32: return digest_rows_sd<S, float>(a, sms, st);
         case DType::BF16: return digest_rows_sd<S, __nv_bfloat16>(a, sms, st);
         case DType::F16: return digest_rows_sd<S, __half>(a, sms, st);
+        default: return cudaErrorInvalidValue;
     }
-    return cudaErrorInvalidValue;
 }
 }  // namespace
 
 cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t st) {
     if (a.num_layers * a.num_tokens * a.entry_elems <= 0) return cudaSuccess;
+    if (a.pool_dtype == DType::FP8_E4M3) return launch_digest_rows_fp8(a, sms, st);
     switch (a.src_dtype) {
         case DType::F32: return digest_rows_s<float>(a, sms, st);
         case DType::BF16: return digest_rows_s<__nv_bfloat16>(a, sms, st);
         case DType::F16: return digest_rows_s<__half>(a, sms, st);
+        default: return cudaErrorInvalidValue;
     }
-    return cudaErrorInvalidValue;
 }
 
 namespace {

@@ -22,9 +22,9 @@ if not LIB_PATH.exists():
 lib = C.CDLL(os.fspath(LIB_PATH))
 
 # pkv_dtype
-F32, BF16, F16 = 0, 1, 2
-DTYPE_TAGS = {"f32": F32, "bf16": BF16, "f16": F16}
-DTYPE_BYTES = {F32: 4, BF16: 2, F16: 2}
+F32, BF16, F16, FP8_E4M3 = 0, 1, 2, 3
+DTYPE_TAGS = {"f32": F32, "bf16": BF16, "f16": F16, "fp8_e4m3": FP8_E4M3}
+DTYPE_BYTES = {F32: 4, BF16: 2, F16: 2, FP8_E4M3: 1}
 
 # pkv_copy_engine
 COPY_AUTO, COPY_VECTOR, COPY_BULK = 0, 1, 2
@@ -65,6 +65,7 @@ _PROTOS = {
     "pkv_copy_blocks_dev": (_I, [_P, _P, _I64, _P]),
     "pkv_zero_blocks_dev": (_I, [_P, _P, _I64, _P]),
     "pkv_set_copy_engine": (_I, [_P, _I]),
+    "pkv_set_kv_scales": (_I, [_P, _P, _P, _U64]),
     "pkv_resolve_slots_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P]),
     "pkv_resolve_and_cache_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P, _P,
                                        _I64, _I64, _I, _P]),

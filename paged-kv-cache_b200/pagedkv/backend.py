@@ -15,7 +15,7 @@ from typing import Iterable, Sequence
 import numpy as np
 
 from . import _lib
-from ._lib import BF16, DTYPE_BYTES, DTYPE_TAGS, F16, F32, lib
+from ._lib import BF16, DTYPE_BYTES, DTYPE_TAGS, F16, F32, FP8_E4M3, lib
 from .config import CacheConfig, PhysicalSlot
 from .errors import from_status
 
@@ -29,17 +29,19 @@ def _check(code: int) -> None:
 
 def _host_array(x, tag: int | None):
     """Contiguous numpy view of a host buffer plus its dtype tag. bf16 data is
-    passed as uint16 bit patterns with tag BF16."""
+    passed as uint16 bit patterns with tag BF16, E4M3 codes as uint8."""
     a = np.ascontiguousarray(x)
     if tag is None:
         if a.dtype in _NP_TAG:
             tag = _NP_TAG[a.dtype]
         elif a.dtype == np.uint16:
             tag = BF16
+        elif a.dtype == np.uint8:
+            tag = FP8_E4M3
         else:
             a = a.astype(np.float32)
             tag = F32
-    expect = {F32: np.float32, F16: np.float16, BF16: np.uint16}[tag]
+    expect = {F32: np.float32, F16: np.float16, BF16: np.uint16, FP8_E4M3: np.uint8}[tag]
     if a.dtype != expect:
         a = a.astype(expect) if tag == F32 else a.view(expect)
     return a, tag
@@ -209,6 +211,14 @@ class B200Backend:
         n = pairs.shape[0] if count is None else count
         _check(lib.pkv_copy_blocks_dev(self._h, _ptr(pairs), n, _stream_ptr(stream)))
 
+    def set_kv_scales(self, k_scales, v_scales) -> None:
+        """Scales of an fp8 (E4M3) pool, [num_layers][num_kv_heads] each (pkv_set_kv_scales)."""
+        ks = np.ascontiguousarray(k_scales, dtype=np.float32).ravel()
+        vs = np.ascontiguousarray(v_scales, dtype=np.float32).ravel()
+        if ks.size != vs.size:
+            raise ValueError("k_scales and v_scales differ in size")
+        _check(lib.pkv_set_kv_scales(self._h, ks.ctypes.data, vs.ctypes.data, ks.size))
+
     def set_copy_engine(self, engine: str) -> None:
         """Engine of later copy_blocks calls: "auto", "vector" or "bulk" (pkv_set_copy_engine)."""
         tag = {"auto": _lib.COPY_AUTO, "vector": _lib.COPY_VECTOR, "bulk": _lib.COPY_BULK}[engine]
@@ -282,12 +292,14 @@ class B200Backend:
         _check(lib.pkv_device_planes(self._h, C.byref(k), C.byref(v)))
         c = self._cfg
         shape = (c.num_layers, c.num_blocks, c.block_size, self.shard_entry_elems)
-        typestr = {F32: "<f4", BF16: "<i2", F16: "<f2"}[self._dtype]
+        typestr = {F32: "<f4", BF16: "<i2", F16: "<f2", FP8_E4M3: "|u1"}[self._dtype]
         out = []
         for p in (k.value, v.value):
             t = torch.as_tensor(_DeviceArray(p or 0, shape, typestr), device=f"cuda:{self.device}")
             if self._dtype == BF16:
                 t = t.view(torch.bfloat16)
+            elif self._dtype == FP8_E4M3:
+                t = t.view(torch.float8_e4m3fn)
             out.append(t)
         return tuple(out)
 
@@ -303,7 +315,8 @@ class B200Backend:
 def _torch_tag(t) -> int:
     import torch
 
-    return {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}[t.dtype]
+    return {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16,
+            torch.float8_e4m3fn: FP8_E4M3}[t.dtype]
 
 
 def _same_layout(k, v) -> None:
