@@ -56,6 +56,9 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="decode: launch instead of graph replay")
     p.add_argument("--unfused", action="store_true",
                    help="resolve slots and scatter in two launches instead of the fused kernel")
+    p.add_argument("--pool-dtype", choices=["bf16", "fp8"], default="bf16",
+                   help="prefill/decode: pool element type; fp8 quantises the bf16 rows to E4M3 "
+                        "with per-(layer, kv head) scales in the same launch")
     p.add_argument("--copy-engine", choices=["auto", "vector", "bulk"], default="auto",
                    help="cow/churn: copy_blocks engine (pkv_set_copy_engine)")
     p.add_argument("--no-e2e", action="store_true")
@@ -301,16 +304,30 @@ def roofline(kernel, alg_bytes, kernel_ms, traffic=None) -> dict:
             "algorithmic_bytes_per_launch": alg_bytes, "kernel_ms": kernel_ms}
 
 
-def check_rows_landed(backend, k, v, d_slots, T, L):
-    """Every token's entry is in its slot (strided sample of tokens, 3 layers)."""
+def check_rows_landed(backend, k, v, d_slots, T, L, inv=None):
+    """Every token's entry is in its slot (strided sample of tokens, 3 layers).
+    For an fp8 pool, `inv` = ([L][heads_here] K, V reciprocal scales): the
+    slot holds E4M3(row * inv), which torch's round-to-nearest-even
+    float8_e4m3fn conversion reproduces for these unsaturated rows."""
     torch = __import__("torch")
     es = k.shape[2]
     pk, pv = backend.planes()
     stride = max(1, T // 4096)
     idx = torch.arange(0, T, stride, device=k.device)
     chk = d_slots[idx]
-    ok = all(torch.equal(pk[l].reshape(-1, es)[chk], k[l, idx]) and
-             torch.equal(pv[l].reshape(-1, es)[chk], v[l, idx]) for l in (0, L // 2, L - 1))
+
+    def want(x, l, plane):
+        if inv is None:
+            return x[l, idx]
+        r = inv[plane][l].repeat_interleave(es // inv[plane].shape[1])
+        return (x[l, idx].float() * r).to(torch.float8_e4m3fn).view(torch.uint8)
+
+    def got(p, l):
+        rows = p[l].reshape(-1, es)[chk]
+        return rows.view(torch.uint8) if inv is not None else rows
+
+    ok = all(torch.equal(got(pk, l), want(k, l, 0)) and torch.equal(got(pv, l), want(v, l, 1))
+             for l in (0, L // 2, L - 1))
     if not ok:
         raise SystemExit("bench: pool contents differ from the inputs")
 
@@ -331,8 +348,27 @@ def wl_table_batch(run, kind: str) -> dict:
     else:
         cfg, tables, ctx, new = build_decode(world)
     T, S = int(new.sum()), len(new)
-    backend = B200Backend(cfg, dtype="bf16", device=run.local, shard_rank=run.rank, num_shards=world)
+    fp8 = args.pool_dtype == "fp8"
+    if fp8:
+        from pagedkv import CacheConfig
+        cfg = CacheConfig(num_blocks=cfg.num_blocks, block_size=cfg.block_size,
+                          num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
+                          num_layers=cfg.num_layers, dtype_bytes=1)
+    backend = B200Backend(cfg, dtype="fp8_e4m3" if fp8 else "bf16", device=run.local,
+                          shard_rank=run.rank, num_shards=world)
     es, L = backend.shard_entry_elems, cfg.num_layers
+    inv = None
+    if fp8:
+        # Seeded per-(layer, kv head) scales in [0.5, 2]; rows here hold this GPU's heads.
+        from pagedkv.workloads import Stream
+        st = Stream(55)
+        n = L * cfg.num_kv_heads
+        sk = st.uniform(n, 0.5, 2.0).astype(np.float32).reshape(L, cfg.num_kv_heads)
+        sv = st.uniform(n, 0.5, 2.0).astype(np.float32).reshape(L, cfg.num_kv_heads)
+        backend.set_kv_scales(sk, sv)
+        h0 = backend.elem_offset // cfg.head_dim
+        h1 = -(-(backend.elem_offset + es) // cfg.head_dim)
+        inv = tuple(torch.from_numpy(np.float32(1.0) / s_[:, h0:h1]).to(dev) for s_ in (sk, sv))
     gen = torch.Generator(device=dev).manual_seed(1000 + run.rank)
     k = torch.randn((L, T, es), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     v = torch.randn((L, T, es), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
@@ -356,7 +392,7 @@ def wl_table_batch(run, kind: str) -> dict:
     run.barrier()
     if backend.device_error() is not None:
         raise SystemExit(f"device error in warm-up: {backend.device_error()}")
-    check_rows_landed(backend, k, v, d_slots, T, L)
+    check_rows_landed(backend, k, v, d_slots, T, L, inv)
 
     graph = None
     if kind == "decode" and not args.no_graph:
@@ -390,7 +426,9 @@ def wl_table_batch(run, kind: str) -> dict:
     K = args.steps
     total_ms, evs, clocks = run.timed_steps(step, K)
     eb = es * 2
-    alg_bytes = T * L * 2 * eb * 2 + T * 8  # read + write K and V, one slot read per token
+    pool_eb = es * (1 if fp8 else 2)
+    # Read K and V rows (bf16) + write them into the pool, one slot per token.
+    alg_bytes = T * L * 2 * (eb + pool_eb) + T * 8
     if graph is None and args.unfused:
         kernel_ms = run.max_over_ranks(_event_ms(evs, 1, 2))
         resolve_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
@@ -424,7 +462,9 @@ def wl_table_batch(run, kind: str) -> dict:
     else:
         workload = f"decode step x{world}: {world}x256 sequences, context U[1,4096], +1 token each"
     workload += (f", Qwen2-7B KV geometry (28 layers, 4 KV heads x 128, bs 16), pool "
-                 f"{cfg.num_blocks} blocks (shuffled free list) head-sharded {world} ways; step = "
+                 f"{cfg.num_blocks} blocks (shuffled free list) head-sharded {world} ways, "
+                 + ("fp8 E4M3 pool (bf16 rows quantised with per-layer, per-head scales)"
+                    if fp8 else "bf16 pool") + "; step = "
                  + ("device slot resolution + all-layer reshape_and_cache" if args.unfused else
                   "slot resolution fused with the all-layer reshape_and_cache (one launch)")
                  + (" replayed as one CUDA graph" if graph is not None else ""))
@@ -439,12 +479,18 @@ def wl_table_batch(run, kind: str) -> dict:
     }, "synthetic (seeded: shuffled free list, " + ("log-uniform prompt lengths" if kind == "prefill"
                                                        else "uniform context lengths") + ", normal K/V)")
     out["gb_per_s"] = alg_bytes * world / (total_ms / K / 1e3) / 1e9
-    kname = ("reshape_copy_kernel (all layers)" if args.unfused else
-             "resolve_cache_kernel (slot resolution fused with the all-layer reshape_and_cache)")
+    if fp8:
+        kname = ("reshape_fp8_kernel (all layers)" if args.unfused else
+                 "resolve_cache_fp8_kernel (slot resolution fused with the all-layer quantising "
+                 "reshape_and_cache)")
+        prof = "reshape_fp8_prefill_ncu" if args.unfused else "resolve_cache_fp8_prefill_ncu"
+    else:
+        kname = ("reshape_copy_kernel (all layers)" if args.unfused else
+                 "resolve_cache_kernel (slot resolution fused with the all-layer reshape_and_cache)")
+        prof = "reshape_prefill_ncu" if args.unfused else "resolve_cache_prefill_ncu"
     out["roofline"] = roofline(kname, alg_bytes, kernel_ms,
-                               profile_traffic("reshape_prefill_ncu" if args.unfused else
-                                               "resolve_cache_prefill_ncu")
-                               if kind == "prefill" else None)
+                               profile_traffic(prof) if kind == "prefill" else None)
+    out["config"]["pool_dtype"] = "fp8_e4m3" if fp8 else "bf16"
     if args.unfused:
         out["resolve_slots_ms"] = resolve_ms
     out["gpu_launches"] = (2 if args.unfused else 1) * K
@@ -458,7 +504,9 @@ def wl_table_batch(run, kind: str) -> dict:
     if run.rank == 0 and world == 1 and not args.no_cpu:
         n = min(4096, T)
         out["cpu_baseline"] = cpu_sample(tables, ctx, new, k[:, :n].float().cpu().numpy(),
-                                         v[:, :n].float().cpu().numpy(), seconds=8.0, threads=1)
+                                         v[:, :n].float().cpu().numpy(), seconds=8.0, threads=1,
+                                         head_dim=cfg.head_dim,
+                                         fp8_scales=(sk, sv) if fp8 else None)
     graph = None  # release the captured graph before its pool is freed
     backend.close()
     return out
@@ -670,7 +718,8 @@ def bench_ops(backend, cfg, dev, stream, reps: int = 10) -> dict:
     peak, _ = measured_peak_gbs()
     es = backend.shard_entry_elems
     L, bs = cfg.num_layers, cfg.block_size
-    block_bytes = bs * es * 2
+    pe = backend.elem_bytes
+    block_bytes = bs * es * pe
     flush = torch.ones(256 * 2**20, dtype=torch.uint8, device=dev)
     st = Stream(77)
     ids = st.permutation(cfg.num_blocks)
@@ -710,7 +759,7 @@ def bench_ops(backend, cfg, dev, stream, reps: int = 10) -> dict:
     kd = torch.randn((L, td, es), device=dev).to(torch.bfloat16)
     sl = torch.from_numpy((ids[600:856] * bs + st.integers(256, 0, bs - 1)).astype(np.int64)).to(dev)
     timed(lambda: backend.reshape_and_cache(kd, kd, sl, stream=stream),
-          td * L * 2 * es * 2 * 2 + td * 8, "decode_reshape_all_layers", {"tokens": td})
+          td * L * 2 * es * (2 + pe) + td * 8, "decode_reshape_all_layers", {"tokens": td})
     assert backend.device_error() is None
     return res
 
@@ -723,7 +772,8 @@ class CpuArm:
 
     NB = 1024
 
-    def __init__(self, tables, ctx, new, kf, vf, threads: int):
+    def __init__(self, tables, ctx, new, kf, vf, threads: int, head_dim: int | None = None,
+                 fp8_scales=None):
         import numpy as np
 
         from oracle.cpu import OracleBackend
@@ -731,11 +781,15 @@ class CpuArm:
 
         L, sample, es = kf.shape
         self.L, self.sample, self.es = L, sample, es
-        cfg = CacheConfig(num_blocks=self.NB, block_size=16, num_kv_heads=1, head_dim=es,
+        hd = head_dim or es
+        cfg = CacheConfig(num_blocks=self.NB, block_size=16, num_kv_heads=es // hd, head_dim=hd,
                           num_layers=L, dtype_bytes=4)
         blocks, offs = host_slots(tables, ctx, new, 16)
         pairs = np.stack([blocks[:sample] % self.NB, offs[:sample]], 1).astype(np.uint64)
         self.orc = OracleBackend(cfg)
+        self.fp8 = fp8_scales is not None
+        if self.fp8:  # the oracle quantises each element, as the device's fp8 path does
+            self.orc.set_fp8(*fp8_scales)
         parts = [p for p in np.array_split(np.arange(sample), threads) if len(p)]
         self.rows = [(np.ascontiguousarray(pairs[p]),
                       [np.ascontiguousarray(kf[l, p]) for l in range(L)],
@@ -762,11 +816,12 @@ class CpuArm:
     def describe(self, passes: int) -> str:
         return (f"{self.sample} tokens x {self.L} layers per pass, {passes} pass(es), f32 planes "
                 f"of {self.NB} blocks x 16 slots x {self.es} (CpuBackend semantics, "
-                "oracle/pkv_oracle.c)")
+                "oracle/pkv_oracle.c" + (", E4M3 quantisation per element)" if self.fp8 else ")"))
 
 
-def cpu_sample(tables, ctx, new, kf, vf, seconds: float, threads: int) -> dict:
-    arm = CpuArm(tables, ctx, new, kf, vf, threads)
+def cpu_sample(tables, ctx, new, kf, vf, seconds: float, threads: int, head_dim=None,
+               fp8_scales=None) -> dict:
+    arm = CpuArm(tables, ctx, new, kf, vf, threads, head_dim, fp8_scales)
     arm.one_pass()
     n = 0
     t0 = time.perf_counter()
