@@ -219,6 +219,33 @@ int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64
                               int64_t layer, const void *k, const void *v,
                               int64_t src_token_stride, int64_t src_layer_stride, int src_dtype,
                               void *stream);
+/* Decode attention over layer `layer` of the pool: one query token per
+ * sequence. No counterpart in the reference, which leaves paged_attention
+ * off its trait until its signature is settled
+ * (crates/paged-kv-core/src/backend.rs:18-22); this one fixes the open
+ * choices as: scores and softmax in f32, output in the pool dtype, and an
+ * optional log-sum-exp per (sequence, head) as the partial softmax state that
+ * chunked prefill merges.
+ *
+ * q and out are [num_seqs][num_q_heads][head_dim] in the pool dtype (bf16 or
+ * f16 pools), q with row pitch q_seq_stride elements (<= 0: dense), out
+ * dense; num_q_heads counts the query heads of the kv heads held by this
+ * backend (a shard must hold whole kv heads) and is a multiple of them: query
+ * head qh reads kv head qh / (num_q_heads / kv_heads), at most 16 per kv
+ * head. Sequence s attends to its context_lens[s] cached tokens, token t in
+ * block block_tables[s][t / 16] slot t % 16 (block_size must be 16; head_dim
+ * 64, 128 or 256). max_context_len bounds every context_lens[s] (a longer one
+ * is recorded as ShapeMismatch in the device error word and yields zeros) and
+ * must fit the tables (<= table_stride * 16). lse (optional, f32
+ * [num_seqs][num_q_heads]) receives log(sum exp(scale * q.k)); an empty
+ * context gives a zero output and lse = -inf. Block ids outside the pool are
+ * recorded (InvalidBlock) and their tokens skipped. */
+int pkv_paged_attention_dev(pkv_backend *b, int64_t layer, const void *q, int64_t q_seq_stride,
+                            int64_t num_seqs, int64_t num_q_heads, const int32_t *block_tables,
+                            int64_t table_stride, const int32_t *context_lens,
+                            int64_t max_context_len, float softmax_scale, void *out, float *lse,
+                            void *stream);
+
 /* Order-independent 64-bit digests of this backend's K and V planes (the
  * element's global index in the full plane and its f32-widened bits, summed;
  * zeros contribute nothing). Digests of the shards of one pool add up

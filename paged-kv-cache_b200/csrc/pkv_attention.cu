@@ -1,0 +1,522 @@
+// pkv_attention.cu -- decode attention over the paged pool: the cache's
+// consumer (the reference leaves `paged_attention` off its trait and lists it
+// as the next kernel: crates/paged-kv-core/src/backend.rs:18-22, README.md
+// roadmap).
+//
+// One new query token per sequence. For sequence s with ctx[s] cached tokens
+// (the new token's K/V already written by reshape_and_cache) and query head
+// qh of kv head h = qh / group:
+//   out[s][qh] = softmax(scale * q[s][qh] . K[s][0..ctx)) . V[s][0..ctx)
+// where token t of the sequence sits in pool block table[s][t / 16], slot
+// t % 16, of layer `layer`.
+//
+// B200 mapping. The work is bounded by HBM (every cached K/V byte of the
+// layer is read once); per token and kv head it is 2 x group x head_dim
+// multiply-adds for QK and again for PV.
+// - Grid (split, kv head, sequence). A split is up to `blocks_per_split`
+//   pool blocks; a short sequence uses fewer splits. Each of the 4 warps of a
+//   CTA takes every 4th block of the split.
+// - Loads: each warp runs its own ring of 3 stages. A stage is one pool
+//   block of one kv head, K then V (16 rows x head_dim), brought from the
+//   pool by TMA tile copies (cp.async.bulk.tensor.2d) straight from the
+//   block table's block id, 128-byte swizzled, completing on an mbarrier.
+//   Waits are bounded.
+// - Math: mma.sync m16n8k16 (bf16 or f16 in, f32 accumulate). The M rows
+//   are the group's query heads (padded to 16), so one K/V tile serves the
+//   whole group. Scores stay in registers; the online softmax rescales the
+//   f32 output accumulators; P is rounded to the input type for the PV
+//   product (as flash attention does).
+// - Warps are merged through shared memory; splits through a small
+//   workspace and a combine kernel (skipped when one split suffices).
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include "pkv_device.cuh"
+#include "pkv_internal.hpp"
+
+namespace pkv {
+namespace {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kAttnStages = 3;
+constexpr int kTok = 16;                 // tokens per pool block
+constexpr int kBoxBytes = kTok * 128;    // one TMA box: 16 rows x 128 bytes
+constexpr int kDeviceCode = 9;           // PKV_ERR_DEVICE
+constexpr long long kAttnWaitCycles = 4000000000ll;  // about 2 s at 2 GHz
+
+template <int D>
+struct AttnGeom {
+    static constexpr int kHalves = D / 64;                    // 128-byte boxes per tile
+    static constexpr int kTileBytes = kHalves * kBoxBytes;    // 16 tokens x D x 2 bytes
+    static constexpr int kStageBytes = 2 * kTileBytes;        // K tile, then V tile
+    static constexpr int kRingBytes = kAttnStages * kStageBytes;
+    static constexpr int kQPitch = (D + 8) * 2;               // padded: conflict-free ldmatrix
+    static constexpr int kQBytes = 16 * kQPitch;
+    static constexpr int kOBytes = kAttnWarps * 16 * D * 4;   // per-warp partial outputs
+    static constexpr int kStatBytes = 2 * kAttnWarps * 16 * 4;
+    static constexpr int kSmem = 1024 + kAttnWarps * kRingBytes + kQBytes;
+    static_assert(kOBytes + kStatBytes <= kAttnWarps * kRingBytes, "combine must fit the rings");
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kAttnWaitCycles) return false;
+    return true;
+}
+
+// One box of a 2-D tensor map (x = element column, y = row) into shared memory.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&c)[4], const uint32_t (&a)[4],
+                                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                 uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Two f32 values as a packed pair of T, `lo` in the low half.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+template <typename T>
+__device__ __forceinline__ T from_float(float x);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_float<__half>(float x) { return __float2half_rn(x); }
+
+// Byte offset of 16-byte chunk `chunk` (of D / 8) of token row `tok` in a K
+// or V tile: the tile is kHalves boxes of 16 rows x 128 bytes, each with the
+// 128-byte TMA swizzle (chunk c of row r stored at chunk c ^ (r mod 8)).
+__device__ __forceinline__ int tile_offset(int tok, int chunk) {
+    return (chunk >> 3) * kBoxBytes + tok * 128 + (((chunk & 7) ^ (tok & 7)) << 4);
+}
+
+// Sequence length as the kernels use it: out-of-range lengths are recorded
+// once and treated as empty.
+__device__ __forceinline__ int checked_ctx(const AttnLaunch &a, int seq, bool report) {
+    const int ctx = __ldg(a.ctx + seq);
+    if (ctx < 0 || ctx > a.max_ctx) {
+        if (report) record_error(a.err, kShapeMismatch, seq);
+        return 0;
+    }
+    return ctx;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kAttnThreads, 2)
+paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                       const AttnLaunch a) {
+    using G = AttnGeom<D>;
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bars[kAttnWarps][kAttnStages];
+    __shared__ int s_failed;
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *qs = smem + kAttnWarps * G::kRingBytes;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    const int ctx = checked_ctx(a, seq, threadIdx.x == 0 && split == 0 && kvh == 0);
+    const int nblk = (ctx + kTok - 1) / kTok;
+    const int b0 = split * a.blocks_per_split;
+    const int b1 = min(nblk, b0 + a.blocks_per_split);
+    if (split > 0 && b0 >= b1) return;  // beyond this sequence's splits: the combine skips it
+
+    // Query tile: row r < group is query head kvh * group + r; other rows zero.
+    const T *q = static_cast<const T *>(a.q) + (long long)seq * a.q_seq_stride + (long long)kvh * a.group * D;
+    for (int i = threadIdx.x; i < 16 * (D / 8); i += kAttnThreads) {
+        const int r = i / (D / 8), c = i - r * (D / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < a.group) v = __ldg(reinterpret_cast<const uint4 *>(q + (long long)r * D) + c);
+        *reinterpret_cast<uint4 *>(qs + r * G::kQPitch + c * 16) = v;
+    }
+    if (lane == 0) {
+        for (int s = 0; s < kAttnStages; ++s) mbar_init(&bars[warp][s]);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x == 0) s_failed = 0;
+    __syncthreads();
+
+    uint32_t qa[D / 16][4];
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+        const int m = lane >> 3, row = ((m & 1) << 3) + (lane & 7);
+        ldsm_x4(qa[ks], qs + row * G::kQPitch + (ks * 2 + (m >> 1)) * 16);
+    }
+
+    unsigned char *ring = smem + warp * G::kRingBytes;
+    const int first = b0 + warp;
+    const int count = first < b1 ? (b1 - first + kAttnWarps - 1) / kAttnWarps : 0;
+    const int *table = a.tables + (long long)seq * a.table_stride;
+
+    // Block id of this warp's item i, broadcast from lane 0; -1 if outside the pool.
+    auto block_of = [&](int i) -> int {
+        int blk = 0;
+        if (lane == 0) blk = __ldg(table + first + kAttnWarps * i);
+        blk = __shfl_sync(0xffffffffu, blk, 0);
+        return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
+    };
+    auto issue = [&](int i) {
+        const int blk = block_of(i);
+        if (blk < 0) {
+            if (lane == 0) record_error(a.err, kInvalidBlock, seq);
+            return;
+        }
+        if (lane == 0) {
+            const int st = i % kAttnStages;
+            unsigned char *buf = ring + st * G::kStageBytes;
+            uint64_t *bar = &bars[warp][st];
+            // Earlier generic-proxy reads and writes of this buffer come
+            // before the async-proxy writes of the copy.
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_expect_tx(bar, (uint32_t)G::kStageBytes);
+            const int y = a.layer_row0 + blk * kTok;
+#pragma unroll
+            for (int hf = 0; hf < G::kHalves; ++hf) {
+                tma_load_2d(buf + hf * kBoxBytes, &tk, kvh * D + hf * 64, y, bar);
+                tma_load_2d(buf + G::kTileBytes + hf * kBoxBytes, &tv, kvh * D + hf * 64, y, bar);
+            }
+        }
+    };
+
+    float o[D / 8][4];
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    uint32_t phase = 0;  // bit s: parity of stage s's next completion
+    bool failed = false;
+
+    int issued = 0;
+    for (; issued < count && issued < kAttnStages; ++issued) issue(issued);
+
+    for (int n = 0; n < issued; ++n) {
+        const int st = n % kAttnStages;
+        const int blk = block_of(n);
+        bool ready = false;
+        if (blk >= 0) {
+            ready = mbar_wait_bounded(&bars[warp][st], (phase >> st) & 1u);
+            phase ^= 1u << st;
+            if (!ready && !failed) {
+                failed = true;  // stop issuing; the loop still waits out the loads in flight
+                if (lane == 0) {
+                    record_error(a.err, kDeviceCode, seq);
+                    s_failed = 1;
+                }
+            }
+        }
+        if (ready && !failed) {
+            const unsigned char *kb = ring + st * G::kStageBytes;
+            unsigned char *vb = ring + st * G::kStageBytes + G::kTileBytes;
+            const int valid = min(kTok, ctx - (first + kAttnWarps * n) * kTok);
+
+            // Scores S[head][token] for the block's 16 tokens (two n-tiles of 8).
+            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+                const int tok = ((lane >> 4) << 3) + (lane & 7);
+                const int chunk = ks * 2 + ((lane >> 3) & 1);
+                uint32_t r[4];
+                ldsm_x4(r, kb + tile_offset(tok, chunk));
+                mma16816<T>(s[0], qa[ks], r[0], r[1]);
+                mma16816<T>(s[1], qa[ks], r[2], r[3]);
+            }
+            // Online softmax in base 2; tokens past the sequence end are masked.
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int tok = nt * 8 + (lane & 3) * 2 + (e & 1);
+                    s[nt][e] = tok < valid ? s[nt][e] * a.scale_log2 : -INFINITY;
+                }
+#pragma unroll
+            for (int rh = 0; rh < 2; ++rh) {
+                float mx = fmaxf(fmaxf(s[0][2 * rh], s[0][2 * rh + 1]), fmaxf(s[1][2 * rh], s[1][2 * rh + 1]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float m_new = fmaxf(m_run[rh], mx);  // finite: token 0 of the block is valid
+                const float corr = exp2f(m_run[rh] - m_new);
+                m_run[rh] = m_new;
+                float sum = 0.f;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 2 * rh; e < 2 * rh + 2; ++e) {
+                        s[nt][e] = exp2f(s[nt][e] - m_new);
+                        sum += s[nt][e];
+                    }
+                l_run[rh] = l_run[rh] * corr + sum;
+#pragma unroll
+                for (int n2 = 0; n2 < D / 8; ++n2) {
+                    o[n2][2 * rh] *= corr;
+                    o[n2][2 * rh + 1] *= corr;
+                }
+            }
+            // Rows past the sequence end may hold anything (even NaN): zero
+            // them in V so that 0-weighted rows contribute exactly 0.
+            if (valid < kTok) {
+                const int rows = kTok - valid;
+                for (int i = lane; i < rows * G::kHalves * 8; i += 32) {
+                    const int r = valid + i / (G::kHalves * 8), c = i % (G::kHalves * 8);
+                    *reinterpret_cast<uint4 *>(vb + (c >> 3) * kBoxBytes + r * 128 + (c & 7) * 16) =
+                        make_uint4(0, 0, 0, 0);
+                }
+                __syncwarp();
+            }
+            // P as the A operand of P.V (rows = heads, k = the block's tokens).
+            uint32_t pa[4] = {pack2<T>(s[0][0], s[0][1]), pack2<T>(s[0][2], s[0][3]),
+                              pack2<T>(s[1][0], s[1][1]), pack2<T>(s[1][2], s[1][3])};
+#pragma unroll
+            for (int n2 = 0; n2 < D / 16; ++n2) {
+                const int tok = (((lane >> 3) & 1) << 3) + (lane & 7);
+                const int chunk = n2 * 2 + (lane >> 4);
+                uint32_t r[4];
+                ldsm_x4_trans(r, vb + tile_offset(tok, chunk));
+                mma16816<T>(o[2 * n2], pa, r[0], r[1]);
+                mma16816<T>(o[2 * n2 + 1], pa, r[2], r[3]);
+            }
+        }
+        __syncwarp();
+        if (!failed && issued < count) issue(issued++);
+    }
+
+    // Per-row sums over the quad that shares a row.
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh) {
+        l_run[rh] += __shfl_xor_sync(0xffffffffu, l_run[rh], 1);
+        l_run[rh] += __shfl_xor_sync(0xffffffffu, l_run[rh], 2);
+    }
+
+    // Merge the four warps through shared memory (the rings are free now).
+    __syncthreads();
+    float *om = reinterpret_cast<float *>(smem);             // [warp][16][D]
+    float *mm = om + kAttnWarps * 16 * D;                     // [warp][16]
+    float *ll = mm + kAttnWarps * 16;                         // [warp][16]
+#pragma unroll
+    for (int n2 = 0; n2 < D / 8; ++n2)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int row = (lane >> 2) + (e >> 1) * 8, d = n2 * 8 + (lane & 3) * 2 + (e & 1);
+            om[(warp * 16 + row) * D + d] = o[n2][e];
+        }
+    if ((lane & 3) == 0) {
+#pragma unroll
+        for (int rh = 0; rh < 2; ++rh) {
+            const int row = (lane >> 2) + rh * 8;
+            mm[warp * 16 + row] = m_run[rh];
+            ll[warp * 16 + row] = l_run[rh];
+        }
+    }
+    __syncthreads();
+    failed = s_failed != 0;  // a timed-out wait in any warp voids the CTA's result
+    for (int idx = threadIdx.x; idx < a.group * D; idx += kAttnThreads) {
+        const int row = idx / D, d = idx - row * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, mm[w * 16 + row]);
+        float L = 0.f, acc = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; ++w) {
+                const float f = exp2f(mm[w * 16 + row] - M);
+                L += ll[w * 16 + row] * f;
+                acc += om[(w * 16 + row) * D + d] * f;
+            }
+        }
+        const float val = (L > 0.f && !failed) ? acc / L : 0.f;
+        const float lse2 = (L > 0.f && !failed) ? M + log2f(L) : -INFINITY;
+        const long long qh = (long long)kvh * a.group + row;
+        const long long sq = (long long)seq * a.num_q_heads + qh;
+        if (a.num_splits == 1) {
+            static_cast<T *>(a.out)[sq * D + d] = from_float<T>(val);
+            if (d == 0 && a.lse) a.lse[sq] = lse2 * 0.69314718055994531f;
+        } else {
+            a.part_o[(sq * a.num_splits + split) * D + d] = val;
+            if (d == 0) a.part_lse[sq * a.num_splits + split] = lse2;
+        }
+    }
+}
+
+// Merges the splits of one (sequence, query head): weights exp2(lse_i - max).
+template <typename T, int D>
+__global__ void __launch_bounds__(D)
+paged_attention_combine_kernel(const AttnLaunch a) {
+    const int qh = blockIdx.x, seq = blockIdx.y, d = threadIdx.x;
+    const int ctx = checked_ctx(a, seq, false);
+    const int nblk = (ctx + kTok - 1) / kTok;
+    const int used = max(1, (nblk + a.blocks_per_split - 1) / a.blocks_per_split);
+    const long long sq = (long long)seq * a.num_q_heads + qh;
+    const float *lse = a.part_lse + sq * a.num_splits;
+    float M = -INFINITY;
+    for (int i = 0; i < used; ++i) M = fmaxf(M, lse[i]);
+    float den = 0.f, acc = 0.f;
+    if (M != -INFINITY) {
+        for (int i = 0; i < used; ++i) {
+            const float w = exp2f(lse[i] - M);
+            den += w;
+            acc += a.part_o[(sq * a.num_splits + i) * D + d] * w;
+        }
+    }
+    static_cast<T *>(a.out)[sq * D + d] = from_float<T>(den > 0.f ? acc / den : 0.f);
+    if (d == 0 && a.lse) a.lse[sq] = den > 0.f ? (M + log2f(den)) * 0.69314718055994531f : -INFINITY;
+}
+
+template <typename T, int D>
+cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t st) {
+    using G = AttnGeom<D>;
+    auto kern = paged_attention_kernel<T, D>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)a.num_splits, (unsigned)a.kv_heads, (unsigned)a.num_seqs);
+    kern<<<grid, kAttnThreads, G::kSmem, st>>>(maps[0], maps[1], a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (a.num_splits > 1) {
+        paged_attention_combine_kernel<T, D>
+            <<<dim3((unsigned)a.num_q_heads, (unsigned)a.num_seqs), D, 0, st>>>(a);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+template <typename T>
+cudaError_t launch_t(const AttnLaunch &a, const CUtensorMap *maps, int head_dim, cudaStream_t st) {
+    switch (head_dim) {
+        case 64: return launch_td<T, 64>(a, maps, st);
+        case 128: return launch_td<T, 128>(a, maps, st);
+        case 256: return launch_td<T, 256>(a, maps, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long long entry_elems,
+                                 long long rows, void *tmaps_out) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (!fn || q != cudaDriverEntryPointSuccess) return cudaErrorNotSupported;
+    auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    const CUtensorMapDataType t =
+        dtype == DType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    // The plane as [rows][entry] elements; a box is 16 rows x 64 elements (128 bytes).
+    const cuuint64_t dims[2] = {(cuuint64_t)entry_elems, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)entry_elems * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)kTok};
+    const cuuint32_t elem_strides[2] = {1, 1};
+    CUtensorMap *maps = static_cast<CUtensorMap *>(tmaps_out);
+    void *planes[2] = {k_plane, v_plane};
+    for (int i = 0; i < 2; ++i) {
+        const CUresult r = encode(&maps[i], t, 2, planes[i], dims, strides, box, elem_strides,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    }
+    return cudaSuccess;
+}
+
+int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split) {
+    const int max_blocks = (max_ctx + kTok - 1) / kTok;
+    // At least one block per warp per split, at most 32 (512 tokens); fewer
+    // blocks per split while the (sequence, kv head) pairs alone cannot fill
+    // two CTAs per SM.
+    int p = 32;
+    while (p > kAttnWarps && num_pairs * ((max_blocks + p - 1) / p) < 2LL * sms) p /= 2;
+    *blocks_per_split = p;
+    return std::max(1, (max_blocks + p - 1) / p);
+}
+
+cudaError_t launch_paged_attention(const AttnLaunch &a, const void *tmaps, DType dtype, int head_dim,
+                                   cudaStream_t st) {
+    if (a.num_seqs <= 0 || a.kv_heads <= 0) return cudaSuccess;
+    const CUtensorMap *maps = static_cast<const CUtensorMap *>(tmaps);
+    switch (dtype) {
+        case DType::BF16: return launch_t<__nv_bfloat16>(a, maps, head_dim, st);
+        case DType::F16: return launch_t<__half>(a, maps, head_dim, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace pkv

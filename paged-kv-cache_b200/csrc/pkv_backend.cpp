@@ -210,6 +210,7 @@ B200Backend::~B200Backend() {
     if (v_plane_) cudaFree(v_plane_);
     if (d_err_) cudaFree(d_err_);
     if (d_inv_) cudaFree(d_inv_);
+    if (d_attn_ws_) cudaFree(d_attn_ws_);
     if (d_stage_) cudaFree(d_stage_);
     if (h_stage_) cudaFreeHost(h_stage_);
     if (h_stage_free_) cudaEventDestroy(h_stage_free_);
@@ -843,6 +844,94 @@ Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_s
         return check("resolve_and_cache", launch_resolve_cache_fp8(a, sms_, st));
     }
     return check("resolve_and_cache", launch_resolve_cache(a, sms_, st));
+}
+
+// Decode attention over one layer (no counterpart in the reference: the
+// trait leaves paged_attention for later, crates/paged-kv-core/src/backend.rs:18-22).
+Status B200Backend::paged_attention_dev(int64_t layer, const void *q, int64_t q_seq_stride,
+                                        int64_t num_seqs, int64_t num_q_heads,
+                                        const int32_t *tables, int64_t table_stride,
+                                        const int32_t *ctx, int64_t max_ctx, float softmax_scale,
+                                        void *out, float *lse, cudaStream_t st) {
+    if (layer < 0 || (uint64_t)layer >= cfg_.num_layers)
+        return error(PKV_ERR_INVALID_LAYER, layer, (int64_t)cfg_.num_layers,
+                     msg_layer((uint64_t)layer, cfg_.num_layers));
+    if (dtype_ != DType::BF16 && dtype_ != DType::F16)
+        return error(PKV_ERR_DEVICE, 0, 0, "paged attention reads bf16 or f16 pools");
+    if (cfg_.block_size != 16)
+        return error(PKV_ERR_DEVICE, 0, 0, "paged attention needs block_size 16");
+    const uint64_t hd = cfg_.head_dim;
+    if (hd != 64 && hd != 128 && hd != 256)
+        return error(PKV_ERR_DEVICE, 0, 0, "paged attention supports head_dim 64, 128 or 256");
+    if (elem_offset() % hd != 0 || shard_entry_ % hd != 0)
+        return error(PKV_ERR_DEVICE, 0, 0, "paged attention needs whole kv heads in this shard");
+    const int64_t kv = (int64_t)(shard_entry_ / hd);
+    if (num_seqs < 0 || num_q_heads <= 0 || num_q_heads % kv != 0)
+        return error(PKV_ERR_SHAPE_MISMATCH, kv, num_q_heads,
+                     "query heads must be a positive multiple of the kv heads held here");
+    const int64_t group = num_q_heads / kv;
+    if (group > 16)
+        return error(PKV_ERR_DEVICE, 0, 0, "paged attention supports at most 16 query heads per kv head");
+    if (num_seqs == 0) return Status::Ok();
+    if (num_seqs > 65535) return error(PKV_ERR_DEVICE, 0, 0, "at most 65535 sequences per call");
+    if (max_ctx < 0 || table_stride < 0 || max_ctx > table_stride * (int64_t)cfg_.block_size ||
+        max_ctx > std::numeric_limits<int32_t>::max() - 16)
+        return error(PKV_ERR_SHAPE_MISMATCH, table_stride * (int64_t)cfg_.block_size, max_ctx,
+                     "max_context_len exceeds the block tables");
+    if (q_seq_stride <= 0) q_seq_stride = num_q_heads * (int64_t)hd;
+    if (q_seq_stride < num_q_heads * (int64_t)hd || q_seq_stride % 8 != 0)
+        return error(PKV_ERR_SHAPE_MISMATCH, num_q_heads * (int64_t)hd, q_seq_stride,
+                     "query row pitch must cover the heads and be a multiple of 8 elements");
+    if (!q || !out || !tables || !ctx) return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+        return error(PKV_ERR_DEVICE, 0, 0, "query and output must be 16-byte aligned");
+    if (!std::isfinite(softmax_scale)) return error(PKV_ERR_DEVICE, 0, 0, "softmax scale must be finite");
+    const long long rows = (long long)(cfg_.num_layers * cfg_.num_blocks * cfg_.block_size);
+    if (rows >= (1ll << 31)) return error(PKV_ERR_DEVICE, 0, 0, "pool too tall for paged attention");
+    DeviceGuard g(device_);
+    cudaError_t e;
+    if (!tmaps_ready_) {
+        if ((e = make_attention_tmaps(k_plane_, v_plane_, dtype_, (long long)shard_entry_, rows,
+                                      tmaps_)) != cudaSuccess)
+            return device_error("building the attention tensor maps", e);
+        tmaps_ready_ = true;
+    }
+    AttnLaunch a{};
+    a.q = q;
+    a.q_seq_stride = q_seq_stride;
+    a.out = out;
+    a.lse = lse;
+    a.tables = tables;
+    a.table_stride = table_stride;
+    a.ctx = ctx;
+    a.num_seqs = (int)num_seqs;
+    a.kv_heads = (int)kv;
+    a.group = (int)group;
+    a.num_q_heads = (int)num_q_heads;
+    a.layer_row0 = (int)(layer * (int64_t)(cfg_.num_blocks * cfg_.block_size));
+    a.num_blocks = (int)cfg_.num_blocks;
+    a.max_ctx = (int)max_ctx;
+    a.num_splits = attention_splits((long long)num_seqs * kv, (int)max_ctx, sms_, &a.blocks_per_split);
+    a.scale_log2 = softmax_scale * 1.4426950408889634f;
+    a.err = d_err_;
+    if (a.num_splits > 1) {
+        const size_t parts = (size_t)num_seqs * num_q_heads * a.num_splits;
+        const size_t need = parts * (hd + 1) * sizeof(float);
+        if (need > d_attn_ws_bytes_) {
+            // The old workspace may still be read by attention work in flight.
+            if ((e = cudaDeviceSynchronize()) != cudaSuccess) return device_error("cudaDeviceSynchronize", e);
+            if (d_attn_ws_) cudaFree(d_attn_ws_);
+            d_attn_ws_ = nullptr;
+            d_attn_ws_bytes_ = 0;
+            const size_t want = std::max(need, d_attn_ws_bytes_ + d_attn_ws_bytes_ / 2);
+            if ((e = cudaMalloc(&d_attn_ws_, want)) != cudaSuccess)
+                return device_error("allocating the attention workspace", e);
+            d_attn_ws_bytes_ = want;
+        }
+        a.part_o = d_attn_ws_;
+        a.part_lse = d_attn_ws_ + parts * hd;
+    }
+    return check("paged_attention", launch_paged_attention(a, tmaps_, dtype_, (int)hd, st));
 }
 
 Status B200Backend::digest(uint64_t *k, uint64_t *v, cudaStream_t st) {

@@ -63,6 +63,10 @@ class B200Backend {
     Status zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t s);
     Status set_copy_engine(int engine);
     Status set_kv_scales(const float *k_scales, const float *v_scales, uint64_t count);
+    Status paged_attention_dev(int64_t layer, const void *q, int64_t q_seq_stride,
+                               int64_t num_seqs, int64_t num_q_heads, const int32_t *tables,
+                               int64_t table_stride, const int32_t *ctx, int64_t max_ctx,
+                               float softmax_scale, void *out, float *lse, cudaStream_t s);
     Status resolve_slots_dev(const int32_t *tables, int64_t table_stride, const int32_t *ctx,
                              const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
                              int32_t *cu, int64_t *slots, cudaStream_t s);
@@ -134,6 +138,12 @@ class B200Backend {
     // reciprocals on the device (K's, then V's).
     std::vector<float> k_scale_, v_scale_;
     float *d_inv_ = nullptr;
+    // Paged attention: TMA descriptors of the K and V planes (built on first
+    // use) and the split workspace (grown on demand).
+    alignas(64) unsigned char tmaps_[256] = {};
+    bool tmaps_ready_ = false;
+    float *d_attn_ws_ = nullptr;
+    size_t d_attn_ws_bytes_ = 0;
     std::string gpu_name_;
 };
 

@@ -186,6 +186,20 @@ int pkv_set_kv_scales(pkv_backend *b, const float *k_scales, const float *v_scal
     return guarded([&] { return b->impl->set_kv_scales(k_scales, v_scales, count); });
 }
 
+int pkv_paged_attention_dev(pkv_backend *b, int64_t layer, const void *q, int64_t q_seq_stride,
+                            int64_t num_seqs, int64_t num_q_heads, const int32_t *block_tables,
+                            int64_t table_stride, const int32_t *context_lens,
+                            int64_t max_context_len, float softmax_scale, void *out, float *lse,
+                            void *stream) {
+    if (!b) return null_handle();
+    return guarded([&] {
+        return b->impl->paged_attention_dev(layer, q, q_seq_stride, num_seqs, num_q_heads,
+                                            block_tables, table_stride, context_lens,
+                                            max_context_len, softmax_scale, out, lse,
+                                            as_stream(stream));
+    });
+}
+
 int pkv_set_copy_engine(pkv_backend *b, int engine) {
     if (!b) return null_handle();
     return guarded([&] { return b->impl->set_copy_engine(engine); });

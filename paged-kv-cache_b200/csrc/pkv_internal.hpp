@@ -156,6 +156,31 @@ struct DigestRowsLaunch {
     Fp8Scales fp8;
 };
 
+// Decode attention over one layer of the pool (pkv_attention.cu): one query
+// token per sequence, GQA groups of `group` query heads per kv head.
+struct AttnLaunch {
+    const void *q;             // [num_seqs][num_q_heads][head_dim], row pitch q_seq_stride
+    long long q_seq_stride;    // elements
+    void *out;                 // [num_seqs][num_q_heads][head_dim], contiguous
+    float *lse;                // [num_seqs][num_q_heads] natural-log sum of exp, or null
+    const int *tables;         // [num_seqs][table_stride]
+    long long table_stride;
+    const int *ctx;            // [num_seqs] tokens in the cache per sequence
+    int num_seqs;
+    int kv_heads;              // kv heads held by this backend
+    int group;                 // query heads per kv head (<= 16)
+    int num_q_heads;           // kv_heads * group
+    int layer_row0;            // layer * num_blocks * block_size: first pool row of the layer
+    int num_blocks;
+    int max_ctx;
+    int blocks_per_split;
+    int num_splits;
+    float scale_log2;          // softmax scale * log2(e)
+    float *part_o;             // [num_seqs][num_q_heads][num_splits][head_dim] when num_splits > 1
+    float *part_lse;           // [num_seqs][num_q_heads][num_splits], base-2
+    DevError *err;
+};
+
 int num_sms(int device);
 
 cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t s);
@@ -169,6 +194,14 @@ cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t s
 cudaError_t launch_resolve_cache(const ResolveCacheLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t s);
+
+// Paged decode attention (pkv_attention.cu). `tmaps` points at two
+// CUtensorMap objects (K plane, V plane) built by make_attention_tmaps.
+cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long long entry_elems,
+                                 long long rows, void *tmaps_out /* 2 x 128 bytes, 64-aligned */);
+int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split);
+cudaError_t launch_paged_attention(const AttnLaunch &a, const void *tmaps, DType dtype,
+                                   int head_dim, cudaStream_t s);
 
 // fp8 (E4M3) pools (pkv_fp8.cu): quantising scatter, fused slot resolution +
 // quantising scatter, and the digests of E4M3 planes and rows.
