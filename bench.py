@@ -47,7 +47,8 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["prefill", "decode", "cow", "churn"], default="prefill",
+    p.add_argument("--workload", choices=["prefill", "decode", "cow", "churn", "attention"],
+                   default="prefill",
                    help="prefill: ragged 65,536-token chunk (headline); decode: 256-sequence "
                         "decode step; cow: beam-search copy-on-write trace; churn: "
                         "continuous-batching trace at 70B-like geometry")
@@ -535,6 +536,105 @@ def build_decode(world: int):
             np.concatenate([p[1] for p in parts]).astype(np.int32))
 
 
+def wl_attention(run) -> dict:
+    """Decode attention over the config-2 batch (256 sequences, context
+    U[1,4096] + the appended token, Qwen2-7B: 28 query heads over 4 kv heads
+    x 128, bf16): one step = paged attention for all 28 layers."""
+    import numpy as np
+
+    torch = run.torch
+    from pagedkv import B200Backend
+
+    args, world, dev, stream = run.args, run.world, run.dev, run.stream
+    cfg, tables, ctx, new = build_decode(world)
+    if args.profile_small:  # the same per-layer launches over a 2-layer pool (2.1 GB), for ncu
+        from pagedkv import CacheConfig
+        cfg = CacheConfig(num_blocks=cfg.num_blocks, block_size=cfg.block_size,
+                          num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, num_layers=2,
+                          dtype_bytes=cfg.dtype_bytes)
+    if cfg.num_kv_heads % world:
+        raise SystemExit("attention workload: kv heads must split evenly over the GPUs")
+    backend = B200Backend(cfg, dtype="bf16", device=run.local, shard_rank=run.rank, num_shards=world)
+    L, D = cfg.num_layers, cfg.head_dim
+    kvh = backend.shard_entry_elems // D
+    hq = kvh * 7  # Qwen2-7B: 28 query heads over 4 kv heads
+    lens = (ctx + new).astype(np.int32)  # the appended token is in the cache too
+    S = len(lens)
+    max_ctx = int(lens.max())
+    gen = torch.Generator(device=dev).manual_seed(3000 + run.rank)
+    with torch.cuda.stream(stream):
+        for p_ in backend.planes():
+            for l in range(L):
+                p_[l].copy_(torch.randn(p_[l].shape, generator=gen, device=dev).to(torch.bfloat16))
+        q = torch.randn((S, hq, D), generator=gen, device=dev).to(torch.bfloat16)
+    stream.synchronize()
+    d_tab = torch.from_numpy(tables).to(dev)
+    d_len = torch.from_numpy(lens).to(dev)
+    out = torch.empty((L, S, hq, D), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((L, S, hq), dtype=torch.float32, device=dev)
+
+    def step(i, ev):
+        if ev is not None:
+            ev.extend(torch.cuda.Event(enable_timing=True) for _ in range(2))
+            ev[0].record(stream)
+        for l in range(L):
+            backend.paged_attention(q, d_tab, d_len, max_ctx, out[l], l, lse=lse[l], stream=stream)
+        if ev is not None:
+            ev[1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step(0, None)
+    stream.synchronize()
+    if backend.device_error() is not None:
+        raise SystemExit(f"device error in attention warm-up: {backend.device_error()}")
+    # Spot check against a float32 torch attention of 8 sequences on 2 layers.
+    kp, vp = backend.planes()
+    worst = 0.0
+    for l in (0, L - 1):
+        for s_ in range(0, S, S // 8):
+            n = int(lens[s_])
+            t = torch.arange(n, device=dev)
+            blk = d_tab[s_, t // 16].long()
+            kk = kp[l, blk, t % 16].float().view(n, kvh, D).repeat_interleave(7, 1)
+            vv = vp[l, blk, t % 16].float().view(n, kvh, D).repeat_interleave(7, 1)
+            sc = torch.einsum("hd,thd->ht", q[s_].float(), kk) * D ** -0.5
+            ref = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), vv)
+            worst = max(worst, float((out[l, s_].float() - ref).abs().max()))
+    if worst > 2e-2:
+        raise SystemExit(f"attention spot check failed: max abs error {worst}")
+
+    K = args.steps
+    total_ms, evs, clocks = run.timed_steps(step, K)
+    kernel_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
+    kv_bytes = int(lens.sum()) * backend.shard_entry_elems * 2 * 2  # K and V, bf16, per layer
+    io_bytes = S * hq * D * 2 * 2 + S * hq * 4 + tables.nbytes + lens.nbytes
+    alg = L * (kv_bytes + io_bytes)
+    workload = (f"decode attention x{world}: {world}x256 sequences, context U[1,4096]+1 "
+                f"(mean {lens.mean():.0f}), Qwen2-7B (28 query heads over 4 kv heads x 128, "
+                f"{L} layers, bs 16, bf16), pool {cfg.num_blocks} blocks head-sharded {world} "
+                "ways; step = paged attention over every layer")
+    out_line = base_line(run, int(lens.sum()) * world * K / (total_ms / 1e3), K, total_ms / K,
+                         "weak", workload, {
+                             "sequences": S, "query_heads_per_gpu": hq, "kv_heads_per_gpu": kvh,
+                             "layers": L, "max_context": max_ctx,
+                             "kv_gib_read_per_step_per_gpu": round(L * kv_bytes / 2**30, 2),
+                             "parallelism": f"kv-head shards x{world}",
+                             "l2": "each step reads %.1f GiB of cache, far more than the 126 MB L2"
+                                   % (L * kv_bytes / 2**30)},
+                         "synthetic (seeded: shuffled free list, uniform context lengths, "
+                         "normal K/V/Q)")
+    out_line["metric"] = "KV tokens attended/s & HBM GB/s (paged decode attention)"
+    out_line["unit"] = "tokens/s"
+    out_line["gb_per_s"] = alg * world / (total_ms / K / 1e3) / 1e9
+    out_line["roofline"] = roofline(f"paged_attention_kernel + combine ({L} layers)", alg, kernel_ms)
+    out_line["gpu_launches"] = K * L * 2
+    out_line["spot_check_max_abs_err"] = worst
+    out_line["clocks"] = clocks
+    backend.close()
+    return out_line
+
+
 def wl_trace(run, kind: str) -> dict:
     """Config 4 (beam-search copy-on-write, Qwen2-7B geometry) or config 5
     (continuous-batching churn, 70B-like geometry): a host trace of StepPlans
@@ -885,6 +985,8 @@ def main():
     run = Run(args)
     if args.workload in ("prefill", "decode"):
         out = wl_table_batch(run, args.workload)
+    elif args.workload == "attention":
+        out = wl_attention(run)
     else:
         out = wl_trace(run, args.workload)
     run.close()

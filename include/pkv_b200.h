@@ -239,7 +239,8 @@ int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64
  * must fit the tables (<= table_stride * 16). lse (optional, f32
  * [num_seqs][num_q_heads]) receives log(sum exp(scale * q.k)); an empty
  * context gives a zero output and lse = -inf. Block ids outside the pool are
- * recorded (InvalidBlock) and their tokens skipped. */
+ * recorded (InvalidBlock) and their tokens skipped. softmax_scale must be
+ * finite and positive. */
 int pkv_paged_attention_dev(pkv_backend *b, int64_t layer, const void *q, int64_t q_seq_stride,
                             int64_t num_seqs, int64_t num_q_heads, const int32_t *block_tables,
                             int64_t table_stride, const int32_t *context_lens,

@@ -24,8 +24,8 @@
 // - Math: mma.sync m16n8k16 (bf16 or f16 in, f32 accumulate). The M rows
 //   are the group's query heads (padded to 16), so one K/V tile serves the
 //   whole group. Scores stay in registers; the online softmax rescales the
-//   f32 output accumulators; P is rounded to the input type for the PV
-//   product (as flash attention does).
+//   f32 output accumulators only when a row maximum rises; P is rounded to
+//   the input type for the PV product (as flash attention does).
 // - Warps are merged through shared memory; splits through a small
 //   workspace and a combine kernel (skipped when one split suffices).
 
@@ -109,16 +109,25 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+// ldmatrix of four 8x8 b16 matrices from a shared-memory address.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(p)));
+                 : "r"(addr));
 }
 
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *p) {
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(p)));
+                 : "r"(addr));
+}
+
+// 2^x by the SFU (PTX ex2.approx.ftz; 2^-inf = +0). The weights it feeds
+// are rounded to bf16/f16 before P.V, far coarser than its error.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 template <typename T>
@@ -164,13 +173,6 @@ template <>
 __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 template <>
 __device__ __forceinline__ __half from_float<__half>(float x) { return __float2half_rn(x); }
-
-// Byte offset of 16-byte chunk `chunk` (of D / 8) of token row `tok` in a K
-// or V tile: the tile is kHalves boxes of 16 rows x 128 bytes, each with the
-// 128-byte TMA swizzle (chunk c of row r stored at chunk c ^ (r mod 8)).
-__device__ __forceinline__ int tile_offset(int tok, int chunk) {
-    return (chunk >> 3) * kBoxBytes + tok * 128 + (((chunk & 7) ^ (tok & 7)) << 4);
-}
 
 // Sequence length as the kernels use it: out-of-range lengths are recorded
 // once and treated as empty.
@@ -222,29 +224,43 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
         const int m = lane >> 3, row = ((m & 1) << 3) + (lane & 7);
-        ldsm_x4(qa[ks], qs + row * G::kQPitch + (ks * 2 + (m >> 1)) * 16);
+        ldsm_x4(qa[ks], smem_u32(qs + row * G::kQPitch + (ks * 2 + (m >> 1)) * 16));
     }
 
     unsigned char *ring = smem + warp * G::kRingBytes;
+    const uint32_t ring_u32 = smem_u32(ring);
     const int first = b0 + warp;
     const int count = first < b1 ? (b1 - first + kAttnWarps - 1) / kAttnWarps : 0;
     const int *table = a.tables + (long long)seq * a.table_stride;
 
-    // Block id of this warp's item i, broadcast from lane 0; -1 if outside the pool.
-    auto block_of = [&](int i) -> int {
+    // ldmatrix row addresses within a tile. Chunk 2*ks + c of row `tok` sits
+    // at box ks / 4, chunk ((2*ks) mod 8) ^ (c ^ (tok mod 8)) (the 128-byte
+    // swizzle), so four offsets per lane cover every k-step; the box is an
+    // immediate added per k-step.
+    uint32_t koff[4], voff[4];
+    {
+        const int kt = ((lane >> 4) << 3) + (lane & 7), kx = ((lane >> 3) & 1) ^ (kt & 7);
+        const int vt = (((lane >> 3) & 1) << 3) + (lane & 7), vx = (lane >> 4) ^ (vt & 7);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            koff[kk] = kt * 128 + (((2 * kk) ^ kx) << 4);
+            voff[kk] = G::kTileBytes + vt * 128 + (((2 * kk) ^ vx) << 4);
+        }
+    }
+
+    uint32_t live = 0;  // bit s: stage s holds a block in flight (block id inside the pool)
+    auto issue = [&](int i) {
+        const int st = i % kAttnStages;
         int blk = 0;
         if (lane == 0) blk = __ldg(table + first + kAttnWarps * i);
         blk = __shfl_sync(0xffffffffu, blk, 0);
-        return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
-    };
-    auto issue = [&](int i) {
-        const int blk = block_of(i);
-        if (blk < 0) {
+        if (blk < 0 || blk >= a.num_blocks) {
             if (lane == 0) record_error(a.err, kInvalidBlock, seq);
+            live &= ~(1u << st);
             return;
         }
+        live |= 1u << st;
         if (lane == 0) {
-            const int st = i % kAttnStages;
             unsigned char *buf = ring + st * G::kStageBytes;
             uint64_t *bar = &bars[warp][st];
             // Earlier generic-proxy reads and writes of this buffer come
@@ -263,7 +279,9 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     float o[D / 8][4];
 #pragma unroll
     for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    // Running row maxima in raw score units (the scale is positive), row sums.
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    const float c = a.scale_log2;
     uint32_t phase = 0;  // bit s: parity of stage s's next completion
     bool failed = false;
 
@@ -272,10 +290,11 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
 
     for (int n = 0; n < issued; ++n) {
         const int st = n % kAttnStages;
-        const int blk = block_of(n);
         bool ready = false;
-        if (blk >= 0) {
-            ready = mbar_wait_bounded(&bars[warp][st], (phase >> st) & 1u);
+        if ((live >> st) & 1u) {
+            uint64_t *bar = &bars[warp][st];
+            const uint32_t par = (phase >> st) & 1u;
+            ready = mbar_try_wait(bar, par) || mbar_wait_bounded(bar, par);
             phase ^= 1u << st;
             if (!ready && !failed) {
                 failed = true;  // stop issuing; the loop still waits out the loads in flight
@@ -286,72 +305,78 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             }
         }
         if (ready && !failed) {
-            const unsigned char *kb = ring + st * G::kStageBytes;
-            unsigned char *vb = ring + st * G::kStageBytes + G::kTileBytes;
+            const uint32_t kb = ring_u32 + st * G::kStageBytes;
             const int valid = min(kTok, ctx - (first + kAttnWarps * n) * kTok);
 
             // Scores S[head][token] for the block's 16 tokens (two n-tiles of 8).
             float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks) {
-                const int tok = ((lane >> 4) << 3) + (lane & 7);
-                const int chunk = ks * 2 + ((lane >> 3) & 1);
                 uint32_t r[4];
-                ldsm_x4(r, kb + tile_offset(tok, chunk));
+                ldsm_x4(r, kb + koff[ks & 3] + (ks >> 2) * kBoxBytes);
                 mma16816<T>(s[0], qa[ks], r[0], r[1]);
                 mma16816<T>(s[1], qa[ks], r[2], r[3]);
             }
-            // Online softmax in base 2; tokens past the sequence end are masked.
+            if (valid < kTok) {
+                // The sequence ends inside this block: mask the tokens past
+                // its end, and zero their V rows (they may hold anything, NaN
+                // included) so that their zero weights contribute exactly 0.
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
+                for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int tok = nt * 8 + (lane & 3) * 2 + (e & 1);
-                    s[nt][e] = tok < valid ? s[nt][e] * a.scale_log2 : -INFINITY;
+                    for (int e = 0; e < 4; ++e)
+                        if (nt * 8 + (lane & 3) * 2 + (e & 1) >= valid) s[nt][e] = -INFINITY;
+                unsigned char *vb = ring + st * G::kStageBytes + G::kTileBytes;
+                for (int i = lane; i < (kTok - valid) * G::kHalves * 8; i += 32) {
+                    const int r = valid + i / (G::kHalves * 8), cc = i % (G::kHalves * 8);
+                    *reinterpret_cast<uint4 *>(vb + (cc >> 3) * kBoxBytes + r * 128 + (cc & 7) * 16) =
+                        make_uint4(0, 0, 0, 0);
                 }
+                __syncwarp();
+            }
+            // Online softmax in base 2: p = 2^((s - m) * c).
+            float m_new[2];
+            bool grew = false;
 #pragma unroll
             for (int rh = 0; rh < 2; ++rh) {
                 float mx = fmaxf(fmaxf(s[0][2 * rh], s[0][2 * rh + 1]), fmaxf(s[1][2 * rh], s[1][2 * rh + 1]));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                const float m_new = fmaxf(m_run[rh], mx);  // finite: token 0 of the block is valid
-                const float corr = exp2f(m_run[rh] - m_new);
-                m_run[rh] = m_new;
-                float sum = 0.f;
+                m_new[rh] = fmaxf(m_run[rh], mx);  // finite: token 0 of the block is valid
+                grew |= m_new[rh] > m_run[rh];
+            }
+            if (__any_sync(0xffffffffu, grew)) {
+                // Some row's maximum rose: rescale its sum and output by 2^((m_old - m_new) * c).
+#pragma unroll
+                for (int rh = 0; rh < 2; ++rh) {
+                    const float corr = ex2((m_run[rh] - m_new[rh]) * c);
+                    l_run[rh] *= corr;
+#pragma unroll
+                    for (int n2 = 0; n2 < D / 8; ++n2) {
+                        o[n2][2 * rh] *= corr;
+                        o[n2][2 * rh + 1] *= corr;
+                    }
+                    m_run[rh] = m_new[rh];
+                }
+            }
+#pragma unroll
+            for (int rh = 0; rh < 2; ++rh) {
+                const float mc = m_run[rh] * c;
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                     for (int e = 2 * rh; e < 2 * rh + 2; ++e) {
-                        s[nt][e] = exp2f(s[nt][e] - m_new);
-                        sum += s[nt][e];
+                        s[nt][e] = ex2(fmaf(s[nt][e], c, -mc));
+                        l_run[rh] += s[nt][e];
                     }
-                l_run[rh] = l_run[rh] * corr + sum;
-#pragma unroll
-                for (int n2 = 0; n2 < D / 8; ++n2) {
-                    o[n2][2 * rh] *= corr;
-                    o[n2][2 * rh + 1] *= corr;
-                }
-            }
-            // Rows past the sequence end may hold anything (even NaN): zero
-            // them in V so that 0-weighted rows contribute exactly 0.
-            if (valid < kTok) {
-                const int rows = kTok - valid;
-                for (int i = lane; i < rows * G::kHalves * 8; i += 32) {
-                    const int r = valid + i / (G::kHalves * 8), c = i % (G::kHalves * 8);
-                    *reinterpret_cast<uint4 *>(vb + (c >> 3) * kBoxBytes + r * 128 + (c & 7) * 16) =
-                        make_uint4(0, 0, 0, 0);
-                }
-                __syncwarp();
             }
             // P as the A operand of P.V (rows = heads, k = the block's tokens).
             uint32_t pa[4] = {pack2<T>(s[0][0], s[0][1]), pack2<T>(s[0][2], s[0][3]),
                               pack2<T>(s[1][0], s[1][1]), pack2<T>(s[1][2], s[1][3])};
 #pragma unroll
             for (int n2 = 0; n2 < D / 16; ++n2) {
-                const int tok = (((lane >> 3) & 1) << 3) + (lane & 7);
-                const int chunk = n2 * 2 + (lane >> 4);
                 uint32_t r[4];
-                ldsm_x4_trans(r, vb + tile_offset(tok, chunk));
+                ldsm_x4_trans(r, kb + voff[n2 & 3] + (n2 >> 2) * kBoxBytes);
                 mma16816<T>(o[2 * n2], pa, r[0], r[1]);
                 mma16816<T>(o[2 * n2 + 1], pa, r[2], r[3]);
             }
@@ -383,7 +408,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
             const int row = (lane >> 2) + rh * 8;
-            mm[warp * 16 + row] = m_run[rh];
+            mm[warp * 16 + row] = m_run[rh] * c;  // base-2 units, as the merge expects
             ll[warp * 16 + row] = l_run[rh];
         }
     }
@@ -499,10 +524,10 @@ cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long
 
 int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split) {
     const int max_blocks = (max_ctx + kTok - 1) / kTok;
-    // At least one block per warp per split, at most 32 (512 tokens); fewer
-    // blocks per split while the (sequence, kv head) pairs alone cannot fill
-    // two CTAs per SM.
-    int p = 32;
+    // At least one block per warp per split, at most 64 (1,024 tokens);
+    // fewer blocks per split while the (sequence, kv head) pairs alone cannot
+    // fill two CTAs per SM.
+    int p = 64;
     while (p > kAttnWarps && num_pairs * ((max_blocks + p - 1) / p) < 2LL * sms) p /= 2;
     *blocks_per_split = p;
     return std::max(1, (max_blocks + p - 1) / p);

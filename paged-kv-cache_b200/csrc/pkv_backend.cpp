@@ -885,7 +885,8 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, int64_t q_
     if (!q || !out || !tables || !ctx) return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
     if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
         return error(PKV_ERR_DEVICE, 0, 0, "query and output must be 16-byte aligned");
-    if (!std::isfinite(softmax_scale)) return error(PKV_ERR_DEVICE, 0, 0, "softmax scale must be finite");
+    if (!std::isfinite(softmax_scale) || !(softmax_scale > 0.0f))
+        return error(PKV_ERR_DEVICE, 0, 0, "softmax scale must be finite and positive");
     const long long rows = (long long)(cfg_.num_layers * cfg_.num_blocks * cfg_.block_size);
     if (rows >= (1ll << 31)) return error(PKV_ERR_DEVICE, 0, 0, "pool too tall for paged attention");
     DeviceGuard g(device_);
