@@ -308,15 +308,23 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             const uint32_t kb = ring_u32 + st * G::kStageBytes;
             const int valid = min(kTok, ctx - (first + kAttnWarps * n) * kTok);
 
-            // Scores S[head][token] for the block's 16 tokens (two n-tiles of 8).
+            // Scores S[head][token] for the block's 16 tokens (two n-tiles of
+            // 8), even and odd k-steps in separate accumulators: four short
+            // dependent mma chains instead of two long ones.
             float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            float s2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks) {
                 uint32_t r[4];
                 ldsm_x4(r, kb + koff[ks & 3] + (ks >> 2) * kBoxBytes);
-                mma16816<T>(s[0], qa[ks], r[0], r[1]);
-                mma16816<T>(s[1], qa[ks], r[2], r[3]);
+                float(&acc)[2][4] = (ks & 1) ? s2 : s;
+                mma16816<T>(acc[0], qa[ks], r[0], r[1]);
+                mma16816<T>(acc[1], qa[ks], r[2], r[3]);
             }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
             if (valid < kTok) {
                 // The sequence ends inside this block: mask the tokens past
                 // its end, and zero their V rows (they may hold anything, NaN
@@ -334,7 +342,11 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 }
                 __syncwarp();
             }
-            // Online softmax in base 2: p = 2^((s - m) * c).
+            // Online softmax in base 2: p = 2^((s - m) * c). The reference
+            // point m moves only when a row's maximum exceeds it by more than
+            // 2^8 in weight, so most blocks skip the rescale; weights stay
+            // below 2^8, which f32 sums and bf16/f16 weights hold with the
+            // same relative precision as weights below 1.
             float m_new[2];
             bool grew = false;
 #pragma unroll
@@ -343,10 +355,11 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
                 m_new[rh] = fmaxf(m_run[rh], mx);  // finite: token 0 of the block is valid
-                grew |= m_new[rh] > m_run[rh];
+                grew |= (m_new[rh] - m_run[rh]) * c > 8.0f;  // true on the first block (m_run = -inf)
             }
             if (__any_sync(0xffffffffu, grew)) {
-                // Some row's maximum rose: rescale its sum and output by 2^((m_old - m_new) * c).
+                // Move every row's reference point to its maximum: rescale its
+                // sum and output by 2^((m_old - m_new) * c).
 #pragma unroll
                 for (int rh = 0; rh < 2; ++rh) {
                     const float corr = ex2((m_run[rh] - m_new[rh]) * c);
