@@ -60,6 +60,9 @@ def parse():
     p.add_argument("--pool-dtype", choices=["bf16", "fp8"], default="bf16",
                    help="prefill/decode: pool element type; fp8 quantises the bf16 rows to E4M3 "
                         "with per-(layer, kv head) scales in the same launch")
+    p.add_argument("--compare-library", action="store_true",
+                   help="attention: also time flashinfer's paged decode (tensor-core path) on "
+                        "the same pool, for comparison")
     p.add_argument("--copy-engine", choices=["auto", "vector", "bulk"], default="auto",
                    help="cow/churn: copy_blocks engine (pkv_set_copy_engine)")
     p.add_argument("--no-e2e", action="store_true")
@@ -604,6 +607,24 @@ def wl_attention(run) -> dict:
     if worst > 2e-2:
         raise SystemExit(f"attention spot check failed: max abs error {worst}")
 
+    graph = None
+    if not args.no_graph:
+        # The step's 2 x L launches replayed as one CUDA graph (the workspace
+        # and tensor maps exist already after the warm-up).
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for l in range(L):
+                backend.paged_attention(q, d_tab, d_len, max_ctx, out[l], l, lse=lse[l], stream=stream)
+        torch.cuda.synchronize()
+
+        def step(i, ev):  # noqa: F811
+            if ev is not None:
+                ev.extend(torch.cuda.Event(enable_timing=True) for _ in range(2))
+                ev[0].record(stream)
+            graph.replay()
+            if ev is not None:
+                ev[1].record(stream)
+
     K = args.steps
     total_ms, evs, clocks = run.timed_steps(step, K)
     kernel_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
@@ -613,7 +634,8 @@ def wl_attention(run) -> dict:
     workload = (f"decode attention x{world}: {world}x256 sequences, context U[1,4096]+1 "
                 f"(mean {lens.mean():.0f}), Qwen2-7B (28 query heads over 4 kv heads x 128, "
                 f"{L} layers, bs 16, bf16), pool {cfg.num_blocks} blocks head-sharded {world} "
-                "ways; step = paged attention over every layer")
+                "ways; step = paged attention over every layer"
+                + (" replayed as one CUDA graph" if graph is not None else ""))
     out_line = base_line(run, int(lens.sum()) * world * K / (total_ms / 1e3), K, total_ms / K,
                          "weak", workload, {
                              "sequences": S, "query_heads_per_gpu": hq, "kv_heads_per_gpu": kvh,
@@ -630,9 +652,62 @@ def wl_attention(run) -> dict:
     out_line["roofline"] = roofline(f"paged_attention_kernel + combine ({L} layers)", alg, kernel_ms)
     out_line["gpu_launches"] = K * L * 2
     out_line["spot_check_max_abs_err"] = worst
+    if args.compare_library and world == 1:
+        out_line["library_comparison"] = flashinfer_decode(backend, q, tables, lens, out, L, stream,
+                                                           kernel_ms / L, kv_bytes)
+    graph = None  # release the captured graph before the backend's buffers go
     out_line["clocks"] = clocks
     backend.close()
     return out_line
+
+
+def flashinfer_decode(backend, q, tables, lens, ours_out, L, stream, ours_layer_ms, kv_bytes):
+    """flashinfer's batched paged decode (tensor-core path, NHD pages) over the
+    same pool layer by layer: the per-layer pool view [num_blocks][16][entry]
+    is its [pages][page_size][kv_heads][head_dim]. Comparison only; nothing of
+    ours runs through it."""
+    import numpy as np
+    import torch
+
+    try:
+        import flashinfer
+    except Exception as ex:  # noqa: BLE001
+        return {"unavailable": repr(ex)[:200]}
+    cfg = backend.config()
+    dev = q.device
+    npages = (lens + 15) // 16
+    indptr = torch.from_numpy(np.concatenate([[0], np.cumsum(npages)]).astype(np.int32)).to(dev)
+    indices = torch.from_numpy(np.concatenate([tables[s_, :npages[s_]] for s_ in range(len(lens))])
+                               .astype(np.int32)).to(dev)
+    last = torch.from_numpy((lens - (npages - 1) * 16).astype(np.int32)).to(dev)
+    kvh = backend.shard_entry_elems // cfg.head_dim
+    ws = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+    w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD", use_tensor_cores=True)
+    w.plan(indptr, indices, last, q.shape[1], kvh, cfg.head_dim, 16, q_data_type=torch.bfloat16,
+           kv_data_type=torch.bfloat16)
+    kp, vp = backend.planes()
+    views = [(kp[l].view(cfg.num_blocks, 16, kvh, cfg.head_dim),
+              vp[l].view(cfg.num_blocks, 16, kvh, cfg.head_dim)) for l in range(L)]
+    with torch.cuda.stream(stream):
+        diff = float((w.run(q, views[0]).float() - ours_out[0].float()).abs().max())
+        for _ in range(3):
+            for l in range(L):
+                w.run(q, views[l])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            for l in range(L):
+                w.run(q, views[l])
+        e1.record(stream)
+    stream.synchronize()
+    ms = e0.elapsed_time(e1) / (5 * L)
+    peak, _ = measured_peak_gbs()
+    return {"library": f"flashinfer {flashinfer.__version__} BatchDecodeWithPagedKVCacheWrapper "
+                       "(tensor cores, NHD)",
+            "layer_ms": ms, "kv_gb_per_s": kv_bytes / ms / 1e6,
+            "kv_frac_of_peak": kv_bytes / ms / 1e6 / peak,
+            "ours_layer_ms": ours_layer_ms, "ours_kv_frac_of_peak": kv_bytes / ours_layer_ms / 1e6 / peak,
+            "max_abs_diff_vs_ours_layer0": diff}
 
 
 def wl_trace(run, kind: str) -> dict:

@@ -248,12 +248,13 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         }
     }
 
+    // This warp's block ids, one per lane (count <= 32: splits hold at most
+    // 128 blocks), read once so that no table load sits in the block loop.
+    const int my_blk = lane < count ? __ldg(table + first + kAttnWarps * lane) : -1;
     uint32_t live = 0;  // bit s: stage s holds a block in flight (block id inside the pool)
     auto issue = [&](int i) {
         const int st = i % kAttnStages;
-        int blk = 0;
-        if (lane == 0) blk = __ldg(table + first + kAttnWarps * i);
-        blk = __shfl_sync(0xffffffffu, blk, 0);
+        const int blk = __shfl_sync(0xffffffffu, my_blk, i);
         if (blk < 0 || blk >= a.num_blocks) {
             if (lane == 0) record_error(a.err, kInvalidBlock, seq);
             live &= ~(1u << st);
@@ -455,28 +456,48 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     }
 }
 
-// Merges the splits of one (sequence, query head): weights exp2(lse_i - max).
+// Merges the splits of one sequence, all its query heads: per head the
+// weights 2^(lse_i - max) / sum go to shared memory, then every thread
+// combines float4 runs of the partial outputs.
 template <typename T, int D>
-__global__ void __launch_bounds__(D)
+__global__ void __launch_bounds__(256)
 paged_attention_combine_kernel(const AttnLaunch a) {
-    const int qh = blockIdx.x, seq = blockIdx.y, d = threadIdx.x;
+    extern __shared__ float s_w[];  // [num_q_heads][num_splits]
+    const int seq = blockIdx.x;
     const int ctx = checked_ctx(a, seq, false);
     const int nblk = (ctx + kTok - 1) / kTok;
     const int used = max(1, (nblk + a.blocks_per_split - 1) / a.blocks_per_split);
-    const long long sq = (long long)seq * a.num_q_heads + qh;
-    const float *lse = a.part_lse + sq * a.num_splits;
-    float M = -INFINITY;
-    for (int i = 0; i < used; ++i) M = fmaxf(M, lse[i]);
-    float den = 0.f, acc = 0.f;
-    if (M != -INFINITY) {
-        for (int i = 0; i < used; ++i) {
-            const float w = exp2f(lse[i] - M);
-            den += w;
-            acc += a.part_o[(sq * a.num_splits + i) * D + d] * w;
-        }
+    for (int h = threadIdx.x; h < a.num_q_heads; h += blockDim.x) {
+        const long long sq = (long long)seq * a.num_q_heads + h;
+        const float *lse = a.part_lse + sq * a.num_splits;
+        float M = -INFINITY;
+        for (int i = 0; i < used; ++i) M = fmaxf(M, lse[i]);
+        float den = 0.f;
+        if (M != -INFINITY)
+            for (int i = 0; i < used; ++i) den += exp2f(lse[i] - M);
+        for (int i = 0; i < used; ++i)
+            s_w[h * a.num_splits + i] = den > 0.f ? exp2f(lse[i] - M) / den : 0.f;
+        if (a.lse) a.lse[sq] = den > 0.f ? (M + log2f(den)) * 0.69314718055994531f : -INFINITY;
     }
-    static_cast<T *>(a.out)[sq * D + d] = from_float<T>(den > 0.f ? acc / den : 0.f);
-    if (d == 0 && a.lse) a.lse[sq] = den > 0.f ? (M + log2f(den)) * 0.69314718055994531f : -INFINITY;
+    __syncthreads();
+    for (int it = threadIdx.x; it < a.num_q_heads * (D / 4); it += blockDim.x) {
+        const int h = it / (D / 4), d4 = it - h * (D / 4);
+        const long long sq = (long long)seq * a.num_q_heads + h;
+        const float4 *po = reinterpret_cast<const float4 *>(a.part_o + sq * a.num_splits * D) + d4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < used; ++i) {
+            const float w = s_w[h * a.num_splits + i];
+            const float4 v = __ldcs(po + i * (D / 4));
+            acc.x += v.x * w;
+            acc.y += v.y * w;
+            acc.z += v.z * w;
+            acc.w += v.w * w;
+        }
+        uint2 packed;
+        packed.x = pack2<T>(acc.x, acc.y);
+        packed.y = pack2<T>(acc.z, acc.w);
+        *reinterpret_cast<uint2 *>(static_cast<T *>(a.out) + sq * D + d4 * 4) = packed;
+    }
 }
 
 template <typename T, int D>
@@ -489,8 +510,13 @@ cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t
     kern<<<grid, kAttnThreads, G::kSmem, st>>>(maps[0], maps[1], a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (a.num_splits > 1) {
-        paged_attention_combine_kernel<T, D>
-            <<<dim3((unsigned)a.num_q_heads, (unsigned)a.num_seqs), D, 0, st>>>(a);
+        const size_t smem = (size_t)a.num_q_heads * a.num_splits * sizeof(float);
+        if (smem > 227 * 1024) return cudaErrorInvalidValue;
+        if (smem > 48 * 1024 &&
+            (e = cudaFuncSetAttribute(paged_attention_combine_kernel<T, D>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+            return e;
+        paged_attention_combine_kernel<T, D><<<(unsigned)a.num_seqs, 256, smem, st>>>(a);
         e = cudaGetLastError();
     }
     return e;
