@@ -122,6 +122,14 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
                  : "r"(addr));
 }
 
+// Transpose of an 8x8 b16 matrix held one row pair per lane (lane t: row
+// t / 4, elements 2(t % 4), +1) into the same layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
 // 2^x by the SFU (PTX ex2.approx.ftz; 2^-inf = +0). The weights it feeds
 // are rounded to bf16/f16 before P.V, far coarser than its error.
 __device__ __forceinline__ float ex2(float x) {
@@ -185,7 +193,7 @@ __device__ __forceinline__ int checked_ctx(const AttnLaunch &a, int seq, bool re
     return ctx;
 }
 
-template <typename T, int D>
+template <typename T, int D, int NT>
 __global__ void __launch_bounds__(kAttnThreads, 2)
 paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                        const AttnLaunch a) {
@@ -220,12 +228,21 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     if (threadIdx.x == 0) s_failed = 0;
     __syncthreads();
 
-    uint32_t qa[D / 16][4];
+    // Queries as the B operand of S^T = K . Q^T: for n-tile nt (query heads
+    // 8nt..8nt+7) and k-step ks, qb = {Q[h][16ks + 2j..], Q[h][16ks + 8 + 2j..]}.
+    uint32_t qb[NT][D / 16][2];
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-        const int m = lane >> 3, row = ((m & 1) << 3) + (lane & 7);
-        ldsm_x4(qa[ks], smem_u32(qs + row * G::kQPitch + (ks * 2 + (m >> 1)) * 16));
-    }
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int kp = 0; kp < D / 32; ++kp) {  // two k-steps per ldmatrix.x4
+            uint32_t r[4];
+            const int row = nt * 8 + (lane & 7);
+            ldsm_x4(r, smem_u32(qs + row * G::kQPitch + (kp * 4 + (lane >> 3)) * 16));
+            qb[nt][2 * kp][0] = r[0];
+            qb[nt][2 * kp][1] = r[1];
+            qb[nt][2 * kp + 1][0] = r[2];
+            qb[nt][2 * kp + 1][1] = r[3];
+        }
 
     unsigned char *ring = smem + warp * G::kRingBytes;
     const uint32_t ring_u32 = smem_u32(ring);
@@ -239,8 +256,12 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     // immediate added per k-step.
     uint32_t koff[4], voff[4];
     {
-        const int kt = ((lane >> 4) << 3) + (lane & 7), kx = ((lane >> 3) & 1) ^ (kt & 7);
-        const int vt = (((lane >> 3) & 1) << 3) + (lane & 7), vx = (lane >> 4) ^ (vt & 7);
+        // K as the A operand of S^T (rows = tokens, k = dims): matrix m of an
+        // x4 load is (tokens 8(m&1).., dims of chunk 2ks + (m>>1)). V^T as the
+        // A operand of O^T (rows = dims, k = tokens), loaded transposed: matrix
+        // m is (tokens 8(m>>1).., dims of chunk 2mt + (m&1)).
+        const int kt = (((lane >> 3) & 1) << 3) + (lane & 7), kx = (lane >> 4) ^ (kt & 7);
+        const int vt = ((lane >> 4) << 3) + (lane & 7), vx = ((lane >> 3) & 1) ^ (vt & 7);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             koff[kk] = kt * 128 + (((2 * kk) ^ kx) << 4);
@@ -277,11 +298,18 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         }
     };
 
-    float o[D / 8][4];
+    // O^T accumulators: o[nt][mt] is the m16n8 tile (dims 16mt.., query heads
+    // 8nt..); this lane holds dims 16mt + g (+8) of heads 8nt + 2j (+1), with
+    // g = lane / 4, j = lane % 4. Running maxima (raw score units; the scale
+    // is positive) and sums per query head: [nt][hc] is head 8nt + 2j + hc.
+    float o[NT][D / 16][4];
 #pragma unroll
-    for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    // Running row maxima in raw score units (the scale is positive), row sums.
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
+    float m_run[NT][2], l_run[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) m_run[nt][0] = m_run[nt][1] = -INFINITY, l_run[nt][0] = l_run[nt][1] = 0.f;
     const float c = a.scale_log2;
     uint32_t phase = 0;  // bit s: parity of stage s's next completion
     bool failed = false;
@@ -309,32 +337,33 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             const uint32_t kb = ring_u32 + st * G::kStageBytes;
             const int valid = min(kTok, ctx - (first + kAttnWarps * n) * kTok);
 
-            // Scores S[head][token] for the block's 16 tokens (two n-tiles of
-            // 8), even and odd k-steps in separate accumulators: four short
-            // dependent mma chains instead of two long ones.
-            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            float s2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            // S^T[token][head] for the block's 16 tokens, even and odd
+            // k-steps in separate accumulators (shorter mma chains).
+            float sc[NT][4], s2[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = s2[nt][0] = s2[nt][1] = s2[nt][2] = s2[nt][3] = 0.f;
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks) {
                 uint32_t r[4];
                 ldsm_x4(r, kb + koff[ks & 3] + (ks >> 2) * kBoxBytes);
-                float(&acc)[2][4] = (ks & 1) ? s2 : s;
-                mma16816<T>(acc[0], qa[ks], r[0], r[1]);
-                mma16816<T>(acc[1], qa[ks], r[2], r[3]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    mma16816<T>((ks & 1) ? s2[nt] : sc[nt], r, qb[nt][ks][0], qb[nt][ks][1]);
             }
+            const int g = lane >> 2;
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
+            for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
+                for (int e = 0; e < 4; ++e) sc[nt][e] += s2[nt][e];
             if (valid < kTok) {
                 // The sequence ends inside this block: mask the tokens past
                 // its end, and zero their V rows (they may hold anything, NaN
                 // included) so that their zero weights contribute exactly 0.
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        if (nt * 8 + (lane & 3) * 2 + (e & 1) >= valid) s[nt][e] = -INFINITY;
+                for (int nt = 0; nt < NT; ++nt) {
+                    if (g >= valid) sc[nt][0] = sc[nt][1] = -INFINITY;
+                    if (g + 8 >= valid) sc[nt][2] = sc[nt][3] = -INFINITY;
+                }
                 unsigned char *vb = ring + st * G::kStageBytes + G::kTileBytes;
                 for (int i = lane; i < (kTok - valid) * G::kHalves * 8; i += 32) {
                     const int r = valid + i / (G::kHalves * 8), cc = i % (G::kHalves * 8);
@@ -343,68 +372,77 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 }
                 __syncwarp();
             }
-            // Online softmax in base 2: p = 2^((s - m) * c). The reference
-            // point m moves only when a row's maximum exceeds it by more than
-            // 2^8 in weight, so most blocks skip the rescale; weights stay
-            // below 2^8, which f32 sums and bf16/f16 weights hold with the
-            // same relative precision as weights below 1.
-            float m_new[2];
+            // Online softmax per query head (a column of S^T, spread over the
+            // 8 lanes with the same j) in base 2: p = 2^((s - m) * c). The
+            // reference point m moves only when a head's maximum exceeds it
+            // by more than 2^8 in weight, so most blocks skip the rescale;
+            // weights stay below 2^8, which f32 sums and bf16/f16 weights hold
+            // with the same relative precision as weights below 1.
+            float m_new[NT][2];
             bool grew = false;
 #pragma unroll
-            for (int rh = 0; rh < 2; ++rh) {
-                float mx = fmaxf(fmaxf(s[0][2 * rh], s[0][2 * rh + 1]), fmaxf(s[1][2 * rh], s[1][2 * rh + 1]));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                m_new[rh] = fmaxf(m_run[rh], mx);  // finite: token 0 of the block is valid
-                grew |= (m_new[rh] - m_run[rh]) * c > 8.0f;  // true on the first block (m_run = -inf)
-            }
-            if (__any_sync(0xffffffffu, grew)) {
-                // Move every row's reference point to its maximum: rescale its
-                // sum and output by 2^((m_old - m_new) * c).
+            for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int rh = 0; rh < 2; ++rh) {
-                    const float corr = ex2((m_run[rh] - m_new[rh]) * c);
-                    l_run[rh] *= corr;
-#pragma unroll
-                    for (int n2 = 0; n2 < D / 8; ++n2) {
-                        o[n2][2 * rh] *= corr;
-                        o[n2][2 * rh + 1] *= corr;
-                    }
-                    m_run[rh] = m_new[rh];
+                for (int hc = 0; hc < 2; ++hc) {
+                    float mx = fmaxf(sc[nt][hc], sc[nt][2 + hc]);
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    m_new[nt][hc] = fmaxf(m_run[nt][hc], mx);  // finite: token 0 is valid
+                    grew |= (m_new[nt][hc] - m_run[nt][hc]) * c > 8.0f;  // always on the first block
                 }
-            }
+            if (__any_sync(0xffffffffu, grew)) {
+                // Move every head's reference point to its maximum: rescale
+                // its sum and output by 2^((m_old - m_new) * c).
 #pragma unroll
-            for (int rh = 0; rh < 2; ++rh) {
-                const float mc = m_run[rh] * c;
+                for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                    for (int hc = 0; hc < 2; ++hc) {
+                        const float corr = ex2((m_run[nt][hc] - m_new[nt][hc]) * c);
+                        l_run[nt][hc] *= corr;
 #pragma unroll
-                    for (int e = 2 * rh; e < 2 * rh + 2; ++e) {
-                        s[nt][e] = ex2(fmaf(s[nt][e], c, -mc));
-                        l_run[rh] += s[nt][e];
+                        for (int mt = 0; mt < D / 16; ++mt) {
+                            o[nt][mt][hc] *= corr;
+                            o[nt][mt][2 + hc] *= corr;
+                        }
+                        m_run[nt][hc] = m_new[nt][hc];
                     }
             }
-            // P as the A operand of P.V (rows = heads, k = the block's tokens).
-            uint32_t pa[4] = {pack2<T>(s[0][0], s[0][1]), pack2<T>(s[0][2], s[0][3]),
-                              pack2<T>(s[1][0], s[1][1]), pack2<T>(s[1][2], s[1][3])};
+            // P^T as the B operand of O^T = V^T . P^T: pack this lane's
+            // weights (tokens g, g+8 of heads 2j, 2j+1) and transpose each
+            // 8x8 half in registers to (tokens 2j.., head g).
+            uint32_t pb[NT][2];
 #pragma unroll
-            for (int n2 = 0; n2 < D / 16; ++n2) {
+            for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    sc[nt][e] = ex2(fmaf(sc[nt][e], c, -m_run[nt][e & 1] * c));
+                    l_run[nt][e & 1] += sc[nt][e];
+                }
+                pb[nt][0] = movmatrix_trans(pack2<T>(sc[nt][0], sc[nt][1]));
+                pb[nt][1] = movmatrix_trans(pack2<T>(sc[nt][2], sc[nt][3]));
+            }
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
                 uint32_t r[4];
-                ldsm_x4_trans(r, kb + voff[n2 & 3] + (n2 >> 2) * kBoxBytes);
-                mma16816<T>(o[2 * n2], pa, r[0], r[1]);
-                mma16816<T>(o[2 * n2 + 1], pa, r[2], r[3]);
+                ldsm_x4_trans(r, kb + voff[mt & 3] + (mt >> 2) * kBoxBytes);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma16816<T>(o[nt][mt], r, pb[nt][0], pb[nt][1]);
             }
         }
         __syncwarp();
         if (!failed && issued < count) issue(issued++);
     }
 
-    // Per-row sums over the quad that shares a row.
+    // Per-head sums over the 8 lanes (g = 0..7) that share a head.
 #pragma unroll
-    for (int rh = 0; rh < 2; ++rh) {
-        l_run[rh] += __shfl_xor_sync(0xffffffffu, l_run[rh], 1);
-        l_run[rh] += __shfl_xor_sync(0xffffffffu, l_run[rh], 2);
-    }
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+            l_run[nt][hc] += __shfl_xor_sync(0xffffffffu, l_run[nt][hc], 4);
+            l_run[nt][hc] += __shfl_xor_sync(0xffffffffu, l_run[nt][hc], 8);
+            l_run[nt][hc] += __shfl_xor_sync(0xffffffffu, l_run[nt][hc], 16);
+        }
 
     // Merge the four warps through shared memory (the rings are free now).
     __syncthreads();
@@ -412,19 +450,23 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     float *mm = om + kAttnWarps * 16 * D;                     // [warp][16]
     float *ll = mm + kAttnWarps * 16;                         // [warp][16]
 #pragma unroll
-    for (int n2 = 0; n2 < D / 8; ++n2)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int row = (lane >> 2) + (e >> 1) * 8, d = n2 * 8 + (lane & 3) * 2 + (e & 1);
-            om[(warp * 16 + row) * D + d] = o[n2][e];
-        }
-    if ((lane & 3) == 0) {
+        for (int mt = 0; mt < D / 16; ++mt)
 #pragma unroll
-        for (int rh = 0; rh < 2; ++rh) {
-            const int row = (lane >> 2) + rh * 8;
-            mm[warp * 16 + row] = m_run[rh] * c;  // base-2 units, as the merge expects
-            ll[warp * 16 + row] = l_run[rh];
-        }
+            for (int e = 0; e < 4; ++e) {
+                const int row = nt * 8 + (lane & 3) * 2 + (e & 1), d = mt * 16 + (lane >> 2) + (e >> 1) * 8;
+                om[(warp * 16 + row) * D + d] = o[nt][mt][e];
+            }
+    if (lane < 4) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {
+                const int row = nt * 8 + lane * 2 + hc;
+                mm[warp * 16 + row] = m_run[nt][hc] * c;  // base-2 units, as the merge expects
+                ll[warp * 16 + row] = l_run[nt][hc];
+            }
     }
     __syncthreads();
     failed = s_failed != 0;  // a timed-out wait in any warp voids the CTA's result
@@ -503,7 +545,7 @@ paged_attention_combine_kernel(const AttnLaunch a) {
 template <typename T, int D>
 cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t st) {
     using G = AttnGeom<D>;
-    auto kern = paged_attention_kernel<T, D>;
+    auto kern = a.group <= 8 ? paged_attention_kernel<T, D, 1> : paged_attention_kernel<T, D, 2>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)a.num_splits, (unsigned)a.kv_heads, (unsigned)a.num_seqs);
