@@ -55,6 +55,9 @@ def parse():
     p.add_argument("--fork-rate", type=float, default=0.05,
                    help="churn: probability per step of forking a running sequence")
     p.add_argument("--no-graph", action="store_true", help="decode: launch instead of graph replay")
+    p.add_argument("--graph-steps", type=int, default=0,
+                   help="decode: steps captured per CUDA graph (0: the largest divisor of "
+                        "--steps up to 8)")
     p.add_argument("--unfused", action="store_true",
                    help="resolve slots and scatter in two launches instead of the fused kernel")
     p.add_argument("--pool-dtype", choices=["bf16", "fp8"], default="bf16",
@@ -398,17 +401,26 @@ def wl_table_batch(run, kind: str) -> dict:
         raise SystemExit(f"device error in warm-up: {backend.device_error()}")
     check_rows_landed(backend, k, v, d_slots, T, L, inv)
 
-    graph = None
+    graph, per_graph = None, 1
     if kind == "decode" and not args.no_graph:
-        # The decode step is launch-bound: replay it as one CUDA graph.
+        # The decode step is launch-bound. An engine replays its whole decode
+        # iteration as one CUDA graph, so the cache write runs back to back
+        # with other kernels; here G consecutive steps are captured in one
+        # graph (each a full launch over all 256 tokens and 28 layers), so
+        # one replay from Python does not cost more than G steps of device work.
+        per_graph = args.graph_steps or max(d for d in range(1, 9) if args.steps % d == 0)
+        if args.steps % per_graph:
+            raise SystemExit(f"--steps {args.steps} is not a multiple of --graph-steps {per_graph}")
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            launch()
+            for _ in range(per_graph):
+                launch()
         torch.cuda.synchronize()
 
     def step(i, ev):
         if graph is not None:
-            graph.replay()
+            if i < 0 or i % per_graph == 0:  # steps i .. i + G - 1 (i = -1: untimed load)
+                graph.replay()
             return
         if ev is not None and args.unfused:
             for _ in range(3):
@@ -440,7 +452,10 @@ def wl_table_batch(run, kind: str) -> dict:
         kernel_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
         resolve_ms = 0.0
     else:
-        # Kernel time inside the graph: the same launch timed on its own.
+        # Kernel time inside the graph: the steps run back to back, so the
+        # device time per step is the kernel plus the gap between launches.
+        # A launch bracketed by events on its own is reported beside it.
+        kernel_ms = total_ms / K
         evs2 = []
         with torch.cuda.stream(stream):
             for _ in range(max(K, 10)):
@@ -450,7 +465,7 @@ def wl_table_batch(run, kind: str) -> dict:
                 e[1].record(stream)
                 evs2.append(e)
         stream.synchronize()
-        kernel_ms = run.max_over_ranks(_event_ms(evs2, 0, 1))
+        single_launch_ms = run.max_over_ranks(_event_ms(evs2, 0, 1))
         resolve_ms = 0.0 if not args.unfused else None
 
     verify = verify_over_group(backend.digest(stream=stream),
@@ -471,7 +486,7 @@ def wl_table_batch(run, kind: str) -> dict:
                     if fp8 else "bf16 pool") + "; step = "
                  + ("device slot resolution + all-layer reshape_and_cache" if args.unfused else
                   "slot resolution fused with the all-layer reshape_and_cache (one launch)")
-                 + (" replayed as one CUDA graph" if graph is not None else ""))
+                 + (f" ({per_graph} steps captured per CUDA graph)" if graph is not None else ""))
     out = base_line(run, T * K / (total_ms / 1e3), K, total_ms / K, "weak", workload, {
         "tokens_per_step": T, "sequences_per_step": S, "layers": L, "entry_elems_per_gpu": es,
         "pool_gib_per_gpu": round(backend.allocated_bytes() / 2**30, 2),
@@ -498,6 +513,9 @@ def wl_table_batch(run, kind: str) -> dict:
     if args.unfused:
         out["resolve_slots_ms"] = resolve_ms
     out["gpu_launches"] = (2 if args.unfused else 1) * K
+    if graph is not None:
+        out["config"]["steps_per_graph"] = per_graph
+        out["single_launch_ms"] = single_launch_ms
     out["verify"] = verify
     out["clocks"] = clocks
     if kind == "prefill" and not args.no_ops and run.rank == 0:
@@ -928,8 +946,16 @@ def bench_ops(backend, cfg, dev, stream, reps: int = 10) -> dict:
           {"pairs": 256, "layers": L, "engine": "cp.async.bulk global->shared->global"})
     backend.set_copy_engine("auto")
     zero = torch.from_numpy(ids[512:576].astype(np.int64)).to(dev)
-    timed(lambda: backend.zero_blocks_dev(zero, stream=stream),
-          64 * L * 2 * block_bytes + 64 * 8, "zero_blocks", {"blocks": 64})
+    zero_big = torch.from_numpy(ids[1024:2048].astype(np.int64)).to(dev)
+    for engine, suffix in (("auto", ""), ("bulk", "_bulk")):
+        backend.set_copy_engine(engine)
+        extra = {"engine": "cp.async.bulk stores of a zeroed shared-memory run"} if suffix else {}
+        timed(lambda: backend.zero_blocks_dev(zero, stream=stream),
+              64 * L * 2 * block_bytes + 64 * 8, "zero_blocks" + suffix, {"blocks": 64, **extra})
+        timed(lambda: backend.zero_blocks_dev(zero_big, stream=stream),
+              1024 * L * 2 * block_bytes + 1024 * 8, "zero_blocks_1024" + suffix,
+              {"blocks": 1024, **extra})
+    backend.set_copy_engine("auto")
     td = 256
     kd = torch.randn((L, td, es), device=dev).to(torch.bfloat16)
     sl = torch.from_numpy((ids[600:856] * bs + st.integers(256, 0, bs - 1)).astype(np.int64)).to(dev)

@@ -188,9 +188,11 @@ typedef enum pkv_copy_engine {
     PKV_COPY_VECTOR = 1,
     PKV_COPY_BULK = 2
 } pkv_copy_engine;
-/* Selects the engine of every later copy_blocks call on this backend (host
- * and device entry points). Unknown engines, and PKV_COPY_BULK for a geometry
- * it cannot take, are rejected with PKV_ERR_DEVICE and leave the engine as it was. */
+/* Selects the engine of every later copy_blocks and zero_blocks call on this
+ * backend (host and device entry points). Under PKV_COPY_BULK, zero_blocks
+ * issues bulk stores of a zeroed shared-memory run; the geometry rule is the
+ * same. Unknown engines, and PKV_COPY_BULK for a geometry it cannot take, are
+ * rejected with PKV_ERR_DEVICE and leave the engine as it was. */
 int pkv_set_copy_engine(pkv_backend *b, int engine);
 /* zero_block (kernels.cu:94-110), batched: blocks = [count] int64 in device memory. */
 int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, void *stream);

@@ -609,7 +609,7 @@ Status B200Backend::launch_zero_ids(const uint64_t *blocks, uint64_t count) {
     a.blocks = static_cast<const long long *>(d_stage_);
     a.num_ids = (long long)count;
     a.err = d_err_;
-    if ((e = launch_zero_blocks(a, stream_)) != cudaSuccess) return device_error("zero_blocks", e);
+    if ((e = launch_zero(a, stream_)) != cudaSuccess) return device_error("zero_blocks", e);
     return Status::Ok();
 }
 
@@ -703,6 +703,11 @@ cudaError_t B200Backend::launch_copy(const CopyLaunch &a, cudaStream_t st) const
     return launch_copy_blocks(a, st);
 }
 
+cudaError_t B200Backend::launch_zero(const ZeroLaunch &a, cudaStream_t st) const {
+    if (copy_engine_ == PKV_COPY_BULK) return launch_zero_blocks_bulk(a, sms_, st);
+    return launch_zero_blocks(a, st);
+}
+
 Status B200Backend::set_copy_engine(int engine) {
     if (engine != PKV_COPY_AUTO && engine != PKV_COPY_VECTOR && engine != PKV_COPY_BULK)
         return error(PKV_ERR_DEVICE, 0, 0, "unknown copy engine " + std::to_string(engine));
@@ -735,7 +740,7 @@ Status B200Backend::zero_blocks_dev(const int64_t *blocks, int64_t count, cudaSt
     a.blocks = reinterpret_cast<const long long *>(blocks);
     a.num_ids = count;
     a.err = d_err_;
-    return check("zero_blocks", launch_zero_blocks(a, st));
+    return check("zero_blocks", launch_zero(a, st));
 }
 
 // Largest sequence count whose prefix fits in one CTA's shared memory.

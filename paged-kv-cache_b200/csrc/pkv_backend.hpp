@@ -108,6 +108,7 @@ class B200Backend {
     Status launch_copy_pairs(const uint64_t *pairs, uint64_t count);
     Status launch_zero_ids(const uint64_t *blocks, uint64_t count);
     cudaError_t launch_copy(const CopyLaunch &a, cudaStream_t st) const;
+    cudaError_t launch_zero(const ZeroLaunch &a, cudaStream_t st) const;
     Fp8Scales fp8_scales() const;
     Status fp8_source_error() const;
     Status upload_inv_scales();

@@ -185,6 +185,56 @@ copy_blocks_bulk_kernel(char *__restrict__ kp, char *__restrict__ vp, long long 
     bulk_wait_all();
 }
 
+// zero_blocks on the same engine. Every CTA fills one chunk of shared
+// memory with zeros, and lane 0 of each warp hands the engine bulk stores of
+// that chunk over its share of the (block, layer, plane, sub-chunk) items:
+// one instruction per up to 32 KiB, with no register data and no loads, so a
+// few hundred issuing lanes keep the write path busy. Ids outside the pool
+// are skipped and recorded. Only the stores' reads of the shared chunk are
+// waited for (the hardware wait on this thread's bulk groups), so the CTA
+// can exit; the writes themselves complete in stream order.
+constexpr int kZeroWarps = 4;
+constexpr int kZeroGroupsInFlight = 8;
+
+__global__ void __launch_bounds__(kZeroWarps * 32)
+zero_blocks_bulk_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_layer,
+                        long long block_bytes, int subs, int chunk_bytes,
+                        const long long *__restrict__ ids, long long num_ids, long long num_blocks,
+                        int num_layers, DevError *err) {
+    extern __shared__ __align__(128) unsigned char zeros[];
+    for (int i = threadIdx.x * 16; i < chunk_bytes; i += blockDim.x * 16)
+        *reinterpret_cast<uint4 *>(zeros + i) = make_uint4(0, 0, 0, 0);
+    // The zeros were written through the generic proxy; the bulk stores read
+    // them through the async proxy.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if ((threadIdx.x & 31) != 0) return;
+
+    const long long items = num_ids * num_layers * 2 * subs;
+    const long long stride = (long long)gridDim.x * kZeroWarps;
+    for (long long x0 = (long long)blockIdx.x * kZeroWarps + (threadIdx.x >> 5); x0 < items;
+         x0 += stride) {
+        long long x = x0;
+        const int sub = (int)(x % subs);
+        x /= subs;
+        const int plane = (int)(x & 1);
+        x >>= 1;
+        const int layer = (int)(x % num_layers);
+        const long long idx = x / num_layers;
+        const long long blk = __ldg(ids + idx);
+        if (blk < 0 || blk >= num_blocks) {
+            if (sub == 0 && plane == 0 && layer == 0) record(err, kInvalidBlock, idx);
+            continue;
+        }
+        bulk_store((plane ? vp : kp) + layer * pool_layer + blk * block_bytes +
+                       (long long)sub * chunk_bytes,
+                   zeros, (uint32_t)chunk_bytes);
+        bulk_commit();
+        asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kZeroGroupsInFlight) : "memory");
+    }
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 }  // namespace
 
 // Bytes moved per bulk copy: the block's plane, or the largest equal part of
@@ -222,6 +272,35 @@ cudaError_t launch_copy_blocks_bulk(const CopyLaunch &a, int sms, cudaStream_t s
         static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool), a.num_blocks * a.block_bytes,
         a.block_bytes, subs, (int)chunk, a.pairs, a.num_pairs, a.num_blocks, (int)a.num_layers,
         a.err);
+    return cudaGetLastError();
+}
+
+}  // namespace pkv
+
+namespace pkv {
+
+bool bulk_zero_supported(const ZeroLaunch &a) {
+    return bulk_chunk_bytes(a.block_bytes) > 0 &&
+           reinterpret_cast<uintptr_t>(a.k_pool) % 16 == 0 &&
+           reinterpret_cast<uintptr_t>(a.v_pool) % 16 == 0;
+}
+
+cudaError_t launch_zero_blocks_bulk(const ZeroLaunch &a, int sms, cudaStream_t st) {
+    if (a.num_ids <= 0 || a.num_layers <= 0 || a.block_bytes <= 0) return cudaSuccess;
+    const long long chunk = bulk_chunk_bytes(a.block_bytes);
+    if (chunk == 0) return cudaErrorInvalidValue;
+    const int subs = (int)(a.block_bytes / chunk);
+    if (chunk > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(zero_blocks_bulk_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk);
+        if (e != cudaSuccess) return e;
+    }
+    const long long items = a.num_ids * a.num_layers * 2 * subs;
+    const long long warps = (long long)sms * 2 * kZeroWarps;  // two CTAs per SM
+    const long long grid = std::max<long long>(1, (std::min(items, warps) + kZeroWarps - 1) / kZeroWarps);
+    zero_blocks_bulk_kernel<<<(unsigned)grid, kZeroWarps * 32, (size_t)chunk, st>>>(
+        static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool), a.num_blocks * a.block_bytes,
+        a.block_bytes, subs, (int)chunk, a.blocks, a.num_ids, a.num_blocks, (int)a.num_layers, a.err);
     return cudaGetLastError();
 }
 

@@ -201,8 +201,8 @@ reshape_fp8_kernel(const char *__restrict__ k, const char *__restrict__ v, long 
 // new_lens, each (token, group) item resolves its slot on chip and quantises
 // its group for every layer of its chunk.
 
-template <typename S, int PER, int UNROLL>
-__global__ void __launch_bounds__(kThreads, 4)
+template <typename S, int PER, int UNROLL, int MIN_CTAS>
+__global__ void __launch_bounds__(kThreads, MIN_CTAS)
 resolve_cache_fp8_kernel(ResolveCacheLaunch a, long long groups, int layers_per_chunk) {
     extern __shared__ int s_cu[];
     __shared__ int s_warp[kThreads / 32];
@@ -370,7 +370,12 @@ cudaError_t resolve_cache_fp8_s(const ResolveCacheLaunch &a, int sms, cudaStream
     const long long bx = std::min<long long>((items + kThreads - 1) / kThreads, (long long)sms * 256);
     dim3 grid((unsigned)std::max<long long>(bx, 1), (unsigned)chunks);
     const size_t smem = (size_t)(a.num_seqs + 1) * sizeof(int);
-    auto kern = g16 ? resolve_cache_fp8_kernel<S, 16, unroll_for<S>()> : resolve_cache_fp8_kernel<S, 1, 1>;
+    // As resolve_cache_kernel: one wave keeps 4 CTAs per SM, larger launches
+    // run at 3 with more registers a thread.
+    const bool one_wave = (long long)grid.x * grid.y <= (long long)sms * 4;
+    auto kern = g16 ? (one_wave ? resolve_cache_fp8_kernel<S, 16, unroll_for<S>(), 4>
+                                : resolve_cache_fp8_kernel<S, 16, unroll_for<S>(), 3>)
+                    : resolve_cache_fp8_kernel<S, 1, 1, 4>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;

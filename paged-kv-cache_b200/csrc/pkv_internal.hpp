@@ -190,6 +190,9 @@ cudaError_t launch_copy_blocks(const CopyLaunch &a, cudaStream_t s);
 bool bulk_copy_supported(const CopyLaunch &a);
 cudaError_t launch_copy_blocks_bulk(const CopyLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_zero_blocks(const ZeroLaunch &a, cudaStream_t s);
+// zero_blocks through the bulk-copy engine (pkv_bulk_copy.cu).
+bool bulk_zero_supported(const ZeroLaunch &a);
+cudaError_t launch_zero_blocks_bulk(const ZeroLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_resolve_slots(const ResolveLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_resolve_cache(const ResolveCacheLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_digest(const DigestLaunch &a, int sms, cudaStream_t s);

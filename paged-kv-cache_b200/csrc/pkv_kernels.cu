@@ -290,8 +290,8 @@ resolve_slots_kernel(const int *__restrict__ tables, long long table_stride,
 // reshape_copy_kernel does. The vector-0 threads of layer chunk 0 also
 // publish the slot (when asked) so attention can use it.
 
-template <typename V, int UNROLL>
-__global__ void __launch_bounds__(kThreads, 4)
+template <typename V, int UNROLL, int MIN_CTAS>
+__global__ void __launch_bounds__(kThreads, MIN_CTAS)
 resolve_cache_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
     extern __shared__ int s_cu[];
     __shared__ int s_warp[kThreads / 32];
@@ -671,13 +671,18 @@ cudaError_t resolve_cache_v(const ResolveCacheLaunch &a, long long entry_bytes, 
     const int lpc = layers_per_chunk(items, a.num_layers, sms, &chunks);
     long long bx = std::min<long long>((items + kThreads - 1) / kThreads, (long long)sms * 256);
     dim3 grid((unsigned)std::max<long long>(bx, 1), (unsigned)chunks);
+    // A launch that fits one wave at 4 CTAs per SM (a decode step) keeps
+    // that residency. Larger ones (a prefill chunk) run at 3 CTAs per SM with
+    // 80 registers a thread: measured on B200, 0.989 of the copy peak against
+    // 0.974 at 4 CTAs per SM and 64 registers.
+    const bool one_wave = (long long)grid.x * grid.y <= (long long)sms * 4;
+    auto kern = one_wave ? resolve_cache_kernel<V, 4, 4> : resolve_cache_kernel<V, 4, 3>;
     const size_t smem = (size_t)(a.num_seqs + 1) * sizeof(int);
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(resolve_cache_kernel<V, 4>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    resolve_cache_kernel<V, 4><<<grid, kThreads, smem, st>>>(a, nvec, lpc);
+    kern<<<grid, kThreads, smem, st>>>(a, nvec, lpc);
     return cudaGetLastError();
 }
 }  // namespace

@@ -119,3 +119,42 @@ def test_bulk_engine_rejects_unaligned_planes(cuda):
     b.copy_blocks([(0, 1)])  # still on the register engine
     with pytest.raises(KeyError):
         b.set_copy_engine("dma")
+
+
+@pytest.mark.parametrize("heads,head_dim", [(4, 128), (12, 128), (1, 64)])
+def test_bulk_engine_zero_blocks(cuda, heads, head_dim):
+    """zero_blocks through bulk stores of a zeroed shared-memory run: 16, 48
+    (two 24 KiB runs) and 2 KiB block planes, many items per issuing lane,
+    repeated ids, and an id outside the pool that is recorded and skipped."""
+    import torch
+
+    cfg = CacheConfig(1200, 16, heads, head_dim, 3, 2)
+    st = Stream(heads * head_dim + 1)
+    gpu = B200Backend(cfg, dtype="bf16")
+    gpu.set_copy_engine("bulk")
+    pk, pv = gpu.planes()
+    g = torch.Generator(device=cuda).manual_seed(heads + head_dim)
+    pk.copy_(torch.randn(pk.shape, device=cuda, generator=g).to(torch.bfloat16))
+    pv.copy_(torch.randn(pv.shape, device=cuda, generator=g).to(torch.bfloat16))
+    ids = st.permutation(cfg.num_blocks)[:700].astype(np.int64)
+    ids[10] = ids[11]  # a repeated id
+    want_k, want_v = pk.clone(), pv.clone()
+    good = torch.from_numpy(ids).to(cuda)
+    want_k[:, good] = 0
+    want_v[:, good] = 0
+    with_bad = np.concatenate([ids[:300], [cfg.num_blocks + 5], ids[300:]])
+    gpu.zero_blocks_dev(torch.from_numpy(with_bad).to(cuda))
+    torch.cuda.synchronize()
+    err = gpu.device_error()
+    assert err is not None and err[1] == 300
+    assert torch.equal(pk.view(torch.int16), want_k.view(torch.int16))
+    assert torch.equal(pv.view(torch.int16), want_v.view(torch.int16))
+    # The host-buffer path on the same engine.
+    more = [int(b) for b in st.permutation(cfg.num_blocks)[:5]]
+    gpu.zero_blocks(more)
+    torch.cuda.synchronize()
+    assert gpu.device_error() is None
+    want_k[:, more] = 0
+    want_v[:, more] = 0
+    assert torch.equal(pk.view(torch.int16), want_k.view(torch.int16))
+    assert torch.equal(pv.view(torch.int16), want_v.view(torch.int16))
