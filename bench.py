@@ -575,7 +575,14 @@ def wl_attention(run) -> dict:
                           dtype_bytes=cfg.dtype_bytes)
     if cfg.num_kv_heads % world:
         raise SystemExit("attention workload: kv heads must split evenly over the GPUs")
-    backend = B200Backend(cfg, dtype="bf16", device=run.local, shard_rank=run.rank, num_shards=world)
+    fp8 = args.pool_dtype == "fp8"
+    if fp8:
+        from pagedkv import CacheConfig
+        cfg = CacheConfig(num_blocks=cfg.num_blocks, block_size=cfg.block_size,
+                          num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
+                          num_layers=cfg.num_layers, dtype_bytes=1)
+    backend = B200Backend(cfg, dtype="fp8_e4m3" if fp8 else "bf16", device=run.local,
+                          shard_rank=run.rank, num_shards=world)
     L, D = cfg.num_layers, cfg.head_dim
     kvh = backend.shard_entry_elems // D
     hq = kvh * 7  # Qwen2-7B: 28 query heads over 4 kv heads
@@ -583,10 +590,23 @@ def wl_attention(run) -> dict:
     S = len(lens)
     max_ctx = int(lens.max())
     gen = torch.Generator(device=dev).manual_seed(3000 + run.rank)
+    h0 = backend.elem_offset // D
+    scales = None
+    if fp8:
+        # Codes of N(0, 3) values with seeded per-(layer, kv head) scales in
+        # [0.2, 0.5]: the cache holds values of about N(0, 1).
+        from pagedkv.workloads import Stream
+        st = Stream(55)
+        n = L * cfg.num_kv_heads
+        sk = st.uniform(n, 0.2, 0.5).astype(np.float32).reshape(L, cfg.num_kv_heads)
+        sv = st.uniform(n, 0.2, 0.5).astype(np.float32).reshape(L, cfg.num_kv_heads)
+        backend.set_kv_scales(sk, sv)
+        scales = tuple(torch.from_numpy(x[:, h0:h0 + kvh]).to(dev) for x in (sk, sv))
     with torch.cuda.stream(stream):
         for p_ in backend.planes():
             for l in range(L):
-                p_[l].copy_(torch.randn(p_[l].shape, generator=gen, device=dev).to(torch.bfloat16))
+                x = torch.randn(p_[l].shape, generator=gen, device=dev)
+                p_[l].copy_((x * 3).to(torch.float8_e4m3fn) if fp8 else x.to(torch.bfloat16))
         q = torch.randn((S, hq, D), generator=gen, device=dev).to(torch.bfloat16)
     stream.synchronize()
     d_tab = torch.from_numpy(tables).to(dev)
@@ -617,8 +637,12 @@ def wl_attention(run) -> dict:
             n = int(lens[s_])
             t = torch.arange(n, device=dev)
             blk = d_tab[s_, t // 16].long()
-            kk = kp[l, blk, t % 16].float().view(n, kvh, D).repeat_interleave(7, 1)
-            vv = vp[l, blk, t % 16].float().view(n, kvh, D).repeat_interleave(7, 1)
+            kk = kp[l, blk, t % 16].float().view(n, kvh, D)
+            vv = vp[l, blk, t % 16].float().view(n, kvh, D)
+            if fp8:  # code * scale per kv head
+                kk = kk * scales[0][l].view(1, kvh, 1)
+                vv = vv * scales[1][l].view(1, kvh, 1)
+            kk, vv = kk.repeat_interleave(7, 1), vv.repeat_interleave(7, 1)
             sc = torch.einsum("hd,thd->ht", q[s_].float(), kk) * D ** -0.5
             ref = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), vv)
             worst = max(worst, float((out[l, s_].float() - ref).abs().max()))
@@ -646,13 +670,14 @@ def wl_attention(run) -> dict:
     K = args.steps
     total_ms, evs, clocks = run.timed_steps(step, K)
     kernel_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
-    kv_bytes = int(lens.sum()) * backend.shard_entry_elems * 2 * 2  # K and V, bf16, per layer
+    kv_bytes = int(lens.sum()) * backend.shard_entry_elems * 2 * backend.elem_bytes  # K and V, per layer
     io_bytes = S * hq * D * 2 * 2 + S * hq * 4 + tables.nbytes + lens.nbytes
     alg = L * (kv_bytes + io_bytes)
     workload = (f"decode attention x{world}: {world}x256 sequences, context U[1,4096]+1 "
                 f"(mean {lens.mean():.0f}), Qwen2-7B (28 query heads over 4 kv heads x 128, "
-                f"{L} layers, bs 16, bf16), pool {cfg.num_blocks} blocks head-sharded {world} "
-                "ways; step = paged attention over every layer"
+                f"{L} layers, bs 16, bf16 queries), pool {cfg.num_blocks} blocks "
+                + ("of E4M3 codes with per-(layer, kv head) scales" if fp8 else "bf16")
+                + f" head-sharded {world} ways; step = paged attention over every layer"
                 + (" replayed as one CUDA graph" if graph is not None else ""))
     out_line = base_line(run, int(lens.sum()) * world * K / (total_ms / 1e3), K, total_ms / K,
                          "weak", workload, {
@@ -670,7 +695,8 @@ def wl_attention(run) -> dict:
     out_line["roofline"] = roofline(f"paged_attention_kernel + combine ({L} layers)", alg, kernel_ms)
     out_line["gpu_launches"] = K * L * 2
     out_line["spot_check_max_abs_err"] = worst
-    if args.compare_library and world == 1:
+    out_line["config"]["pool_dtype"] = "fp8_e4m3" if fp8 else "bf16"
+    if args.compare_library and world == 1 and not fp8:
         out_line["library_comparison"] = flashinfer_decode(backend, q, tables, lens, out, L, stream,
                                                            kernel_ms / L, kv_bytes)
     graph = None  # release the captured graph before the backend's buffers go

@@ -248,6 +248,19 @@ int pkv_paged_attention_dev(pkv_backend *b, int64_t layer, const void *q, int64_
                             int64_t table_stride, const int32_t *context_lens,
                             int64_t max_context_len, float softmax_scale, void *out, float *lse,
                             void *stream);
+/* pkv_paged_attention_dev with the type of q and out given (a pkv_dtype):
+ * over a bf16 or f16 pool it must be the pool dtype; over an fp8 (E4M3) pool
+ * it is PKV_BF16 or PKV_F16, and attention reads the dequantised cache,
+ * code * scale with the per-(layer, kv head) scales of pkv_set_kv_scales.
+ * The codes enter the tensor cores as f16 (exact for every E4M3 value), and
+ * so do the queries, scaled by a power of two into f16 range; the scores,
+ * softmax and output accumulate in f32. Otherwise as pkv_paged_attention_dev.
+ * No counterpart in the reference (no attention, no fp8 format). */
+int pkv_paged_attention_typed_dev(pkv_backend *b, int64_t layer, const void *q, int query_dtype,
+                                  int64_t q_seq_stride, int64_t num_seqs, int64_t num_q_heads,
+                                  const int32_t *block_tables, int64_t table_stride,
+                                  const int32_t *context_lens, int64_t max_context_len,
+                                  float softmax_scale, void *out, float *lse, void *stream);
 
 /* Order-independent 64-bit digests of this backend's K and V planes (the
  * element's global index in the full plane and its f32-widened bits, summed;

@@ -35,9 +35,11 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <type_traits>
 
 #include "pkv_device.cuh"
 #include "pkv_internal.hpp"
@@ -47,24 +49,41 @@ namespace {
 
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
-constexpr int kAttnStages = 3;
+constexpr int kMaxStages = 6;
 constexpr int kTok = 16;                 // tokens per pool block
-constexpr int kBoxBytes = kTok * 128;    // one TMA box: 16 rows x 128 bytes
 constexpr int kDeviceCode = 9;           // PKV_ERR_DEVICE
 constexpr long long kAttnWaitCycles = 4000000000ll;  // about 2 s at 2 GHz
 
-template <int D>
+// Tile geometry. A tile is one pool block of one kv head: 16 rows of D
+// elements, brought in as boxes of 16 rows x up to 128 bytes, swizzled in
+// 16-byte chunks (128-byte rows: chunk c of row r at c ^ (r % 8); the 64-byte
+// rows of a 64-dim fp8 head: c ^ ((r / 2) % 4)). fp8 tiles are half as big,
+// so three stages a warp leave room for four CTAs per SM: the same bytes in
+// flight as two CTAs of bf16 tiles, and 16 warps to hide the conversions.
+template <int D, bool FP8>
 struct AttnGeom {
-    static constexpr int kHalves = D / 64;                    // 128-byte boxes per tile
-    static constexpr int kTileBytes = kHalves * kBoxBytes;    // 16 tokens x D x 2 bytes
-    static constexpr int kStageBytes = 2 * kTileBytes;        // K tile, then V tile
-    static constexpr int kRingBytes = kAttnStages * kStageBytes;
+    static constexpr int kElemBytes = FP8 ? 1 : 2;
+    static constexpr int kRowBytes = D * kElemBytes;                       // one head's row
+    static constexpr int kBoxRow = kRowBytes < 128 ? kRowBytes : 128;      // bytes per box row
+    static constexpr int kBoxElems = kBoxRow / kElemBytes;
+    static constexpr int kBoxes = kRowBytes / kBoxRow;                     // boxes per tile
+    static constexpr int kBoxBytes = kTok * kBoxRow;
+    static constexpr int kTileBytes = kBoxes * kBoxBytes;                  // 16 tokens x D elements
+    static constexpr int kStages = 3;
+    static constexpr int kStageBytes = 2 * kTileBytes;                     // K tile, then V tile
+    static constexpr int kRingBytes = kStages * kStageBytes;
     static constexpr int kQPitch = (D + 8) * 2;               // padded: conflict-free ldmatrix
     static constexpr int kQBytes = 16 * kQPitch;
     static constexpr int kOBytes = kAttnWarps * 16 * D * 4;   // per-warp partial outputs
     static constexpr int kStatBytes = 2 * kAttnWarps * 16 * 4;
     static constexpr int kSmem = 1024 + kAttnWarps * kRingBytes + kQBytes;
+    static_assert(kStages <= kMaxStages, "stage masks");
     static_assert(kOBytes + kStatBytes <= kAttnWarps * kRingBytes, "combine must fit the rings");
+
+    // Byte offset of 16-byte chunk c of row r within a box.
+    __device__ static constexpr int chunk_at(int r, int c) {
+        return kBoxRow == 128 ? r * 128 + ((c ^ (r & 7)) << 4) : r * kBoxRow + ((c ^ ((r >> 1) & 3)) << 4);
+    }
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -138,6 +157,17 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Four E4M3 codes (byte 0 first) as two f16 pairs: bytes 0, 1 -> lo (byte 0
+// in the low half), bytes 2, 3 -> hi. Exact: every E4M3 value is an f16 value.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t codes, uint32_t &lo, uint32_t &hi) {
+    asm("{\n\t.reg .b16 a, b;\n\t"
+        "mov.b32 {a, b}, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, a;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+        : "=r"(lo), "=r"(hi)
+        : "r"(codes));
+}
+
 template <typename T>
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
 
@@ -175,6 +205,9 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&v);
 }
 
+__device__ __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_float(__half x) { return __half2float(x); }
+
 template <typename T>
 __device__ __forceinline__ T from_float(float x);
 template <>
@@ -193,14 +226,21 @@ __device__ __forceinline__ int checked_ctx(const AttnLaunch &a, int seq, bool re
     return ctx;
 }
 
-template <typename T, int D, int NT>
-__global__ void __launch_bounds__(kAttnThreads, 2)
+// T: query and output type. FP8: the pool holds E4M3 codes with per-(layer,
+// kv head) scales; the tiles are converted to f16 in registers and the math
+// runs in f16 (queries too, scaled by a power of two into f16 range), with
+// the K scale folded into the softmax scale and the V scale into the output.
+template <typename T, int D, int NT, bool FP8>
+__global__ void __launch_bounds__(kAttnThreads, (FP8 && D <= 128) ? (NT == 1 ? 4 : 3) : 2)
 paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                        const AttnLaunch a) {
-    using G = AttnGeom<D>;
+    using G = AttnGeom<D, FP8>;
+    using C = std::conditional_t<FP8, __half, T>;  // tensor-core operand type
+    constexpr int kStages = G::kStages;
     extern __shared__ unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t bars[kAttnWarps][kAttnStages];
+    __shared__ __align__(8) uint64_t bars[kAttnWarps][kStages];
     __shared__ int s_failed;
+    __shared__ int s_qmax;  // fp8: max |q| of the group, as f32 bits
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *qs = smem + kAttnWarps * G::kRingBytes;
@@ -215,14 +255,56 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
 
     // Query tile: row r < group is query head kvh * group + r; other rows zero.
     const T *q = static_cast<const T *>(a.q) + (long long)seq * a.q_seq_stride + (long long)kvh * a.group * D;
-    for (int i = threadIdx.x; i < 16 * (D / 8); i += kAttnThreads) {
-        const int r = i / (D / 8), c = i - r * (D / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < a.group) v = __ldg(reinterpret_cast<const uint4 *>(q + (long long)r * D) + c);
-        *reinterpret_cast<uint4 *>(qs + r * G::kQPitch + c * 16) = v;
+    float c = a.scale_log2;
+    float v_scale = 1.f;
+    if constexpr (FP8) {
+        // f16 holds every E4M3 code exactly; the queries are brought into
+        // its range by 2^-e (e > 0 only when some |q| >= 2^14), and 2^e
+        // joins the K scale in the softmax scale.
+        if (threadIdx.x == 0) s_qmax = 0;
+        __syncthreads();
+        float mx = 0.f;
+        for (int i = threadIdx.x; i < a.group * (D / 8); i += kAttnThreads) {
+            const int r = i / (D / 8), cc = i - r * (D / 8);
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(q + (long long)r * D) + cc);
+            const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(to_float(e[k])));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) atomicMax(&s_qmax, __float_as_int(mx));  // non-negative: int order
+        __syncthreads();
+        const float qmax = __int_as_float(s_qmax);
+        int ex = 0;
+        if (qmax < INFINITY) frexpf(qmax, &ex);
+        const int e = max(0, ex - 14);
+        const float down = ldexpf(1.f, -e);
+        c *= __ldg(a.k_scale + a.scale_row + kvh) * ldexpf(1.f, e);
+        v_scale = __ldg(a.v_scale + a.scale_row + kvh);
+        for (int i = threadIdx.x; i < 16 * (D / 8); i += kAttnThreads) {
+            const int r = i / (D / 8), cc = i - r * (D / 8);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < a.group) {
+                const uint4 x = __ldg(reinterpret_cast<const uint4 *>(q + (long long)r * D) + cc);
+                const T *xe = reinterpret_cast<const T *>(&x);
+                uint32_t *w = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    w[k] = pack2<__half>(to_float(xe[2 * k]) * down, to_float(xe[2 * k + 1]) * down);
+            }
+            *reinterpret_cast<uint4 *>(qs + r * G::kQPitch + cc * 16) = v;
+        }
+    } else {
+        for (int i = threadIdx.x; i < 16 * (D / 8); i += kAttnThreads) {
+            const int r = i / (D / 8), cc = i - r * (D / 8);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < a.group) v = __ldg(reinterpret_cast<const uint4 *>(q + (long long)r * D) + cc);
+            *reinterpret_cast<uint4 *>(qs + r * G::kQPitch + cc * 16) = v;
+        }
     }
     if (lane == 0) {
-        for (int s = 0; s < kAttnStages; ++s) mbar_init(&bars[warp][s]);
+        for (int s = 0; s < kStages; ++s) mbar_init(&bars[warp][s]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x == 0) s_failed = 0;
@@ -230,19 +312,33 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
 
     // Queries as the B operand of S^T = K . Q^T: for n-tile nt (query heads
     // 8nt..8nt+7) and k-step ks, qb = {Q[h][16ks + 2j..], Q[h][16ks + 8 + 2j..]}.
+    // fp8 tiles order each k-step's 16 dims as the K fragments arrive
+    // (below): logical k 2j, 2j+1 are dims 4j, 4j+1 and logical k 2j+8, 2j+9
+    // are dims 4j+2, 4j+3, so qb = Q[h][16ks + 4j .. 16ks + 4j + 3].
     uint32_t qb[NT][D / 16][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt) {
+        if constexpr (FP8) {
 #pragma unroll
-        for (int kp = 0; kp < D / 32; ++kp) {  // two k-steps per ldmatrix.x4
-            uint32_t r[4];
-            const int row = nt * 8 + (lane & 7);
-            ldsm_x4(r, smem_u32(qs + row * G::kQPitch + (kp * 4 + (lane >> 3)) * 16));
-            qb[nt][2 * kp][0] = r[0];
-            qb[nt][2 * kp][1] = r[1];
-            qb[nt][2 * kp + 1][0] = r[2];
-            qb[nt][2 * kp + 1][1] = r[3];
+            for (int ks = 0; ks < D / 16; ++ks) {
+                const uint2 w = *reinterpret_cast<const uint2 *>(
+                    qs + (nt * 8 + (lane >> 2)) * G::kQPitch + (ks * 16 + (lane & 3) * 4) * 2);
+                qb[nt][ks][0] = w.x;
+                qb[nt][ks][1] = w.y;
+            }
+        } else {
+#pragma unroll
+            for (int kp = 0; kp < D / 32; ++kp) {  // two k-steps per ldmatrix.x4
+                uint32_t r[4];
+                const int row = nt * 8 + (lane & 7);
+                ldsm_x4(r, smem_u32(qs + row * G::kQPitch + (kp * 4 + (lane >> 3)) * 16));
+                qb[nt][2 * kp][0] = r[0];
+                qb[nt][2 * kp][1] = r[1];
+                qb[nt][2 * kp + 1][0] = r[2];
+                qb[nt][2 * kp + 1][1] = r[3];
+            }
         }
+    }
 
     unsigned char *ring = smem + warp * G::kRingBytes;
     const uint32_t ring_u32 = smem_u32(ring);
@@ -250,16 +346,27 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     const int count = first < b1 ? (b1 - first + kAttnWarps - 1) / kAttnWarps : 0;
     const int *table = a.tables + (long long)seq * a.table_stride;
 
-    // ldmatrix row addresses within a tile. Chunk 2*ks + c of row `tok` sits
-    // at box ks / 4, chunk ((2*ks) mod 8) ^ (c ^ (tok mod 8)) (the 128-byte
-    // swizzle), so four offsets per lane cover every k-step; the box is an
-    // immediate added per k-step.
-    uint32_t koff[4], voff[4];
-    {
-        // K as the A operand of S^T (rows = tokens, k = dims): matrix m of an
-        // x4 load is (tokens 8(m&1).., dims of chunk 2ks + (m>>1)). V^T as the
-        // A operand of O^T (rows = dims, k = tokens), loaded transposed: matrix
-        // m is (tokens 8(m>>1).., dims of chunk 2mt + (m&1)).
+    // ldmatrix row addresses within a tile; the box is an immediate added
+    // per step.
+    //  bf16/f16: chunk 2*ks + c of row `tok` sits at box ks / 4, chunk
+    //  ((2*ks) mod 8) ^ (c ^ (tok mod 8)), so four offsets per lane cover
+    //  every k-step. K is the A operand of S^T (rows = tokens, k = dims):
+    //  matrix m of an x4 load is (tokens 8(m&1).., dims of chunk 2ks + (m>>1)).
+    //  V^T is the A operand of O^T (rows = dims, k = tokens), loaded
+    //  transposed: matrix m is (tokens 8(m>>1).., dims of chunk 2mt + (m&1)).
+    //  fp8: a 16-byte chunk is 16 dims of a token; one x4 load (as b16 pairs)
+    //  covers chunks 2p, 2p+1: matrix m is (tokens 8(m&1).., chunk 2p + (m>>1)),
+    //  the same addresses for K and (transposed) for V.
+    constexpr int kOffs = FP8 ? (G::kBoxRow / 32 < 1 ? 1 : G::kBoxRow / 32) : 4;
+    uint32_t koff[kOffs], voff[kOffs];
+    if constexpr (FP8) {
+        const int tok = (lane & 7) + (((lane >> 3) & 1) << 3), half = lane >> 4;
+#pragma unroll
+        for (int pp = 0; pp < kOffs; ++pp) {
+            koff[pp] = G::chunk_at(tok, 2 * pp + half);
+            voff[pp] = G::kTileBytes + koff[pp];
+        }
+    } else {
         const int kt = (((lane >> 3) & 1) << 3) + (lane & 7), kx = (lane >> 4) ^ (kt & 7);
         const int vt = ((lane >> 4) << 3) + (lane & 7), vx = ((lane >> 3) & 1) ^ (vt & 7);
 #pragma unroll
@@ -274,7 +381,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     const int my_blk = lane < count ? __ldg(table + first + kAttnWarps * lane) : -1;
     uint32_t live = 0;  // bit s: stage s holds a block in flight (block id inside the pool)
     auto issue = [&](int i) {
-        const int st = i % kAttnStages;
+        const int st = i % kStages;
         const int blk = __shfl_sync(0xffffffffu, my_blk, i);
         if (blk < 0 || blk >= a.num_blocks) {
             if (lane == 0) record_error(a.err, kInvalidBlock, seq);
@@ -291,17 +398,18 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             mbar_expect_tx(bar, (uint32_t)G::kStageBytes);
             const int y = a.layer_row0 + blk * kTok;
 #pragma unroll
-            for (int hf = 0; hf < G::kHalves; ++hf) {
-                tma_load_2d(buf + hf * kBoxBytes, &tk, kvh * D + hf * 64, y, bar);
-                tma_load_2d(buf + G::kTileBytes + hf * kBoxBytes, &tv, kvh * D + hf * 64, y, bar);
+            for (int hf = 0; hf < G::kBoxes; ++hf) {
+                tma_load_2d(buf + hf * G::kBoxBytes, &tk, kvh * D + hf * G::kBoxElems, y, bar);
+                tma_load_2d(buf + G::kTileBytes + hf * G::kBoxBytes, &tv, kvh * D + hf * G::kBoxElems, y, bar);
             }
         }
     };
 
     // O^T accumulators: o[nt][mt] is the m16n8 tile (dims 16mt.., query heads
     // 8nt..); this lane holds dims 16mt + g (+8) of heads 8nt + 2j (+1), with
-    // g = lane / 4, j = lane % 4. Running maxima (raw score units; the scale
-    // is positive) and sums per query head: [nt][hc] is head 8nt + 2j + hc.
+    // g = lane / 4, j = lane % 4 (fp8: dims 16mt + 2g (+1), the order the V
+    // fragments arrive in). Running maxima (raw score units; the scale is
+    // positive) and sums per query head: [nt][hc] is head 8nt + 2j + hc.
     float o[NT][D / 16][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -310,15 +418,14 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     float m_run[NT][2], l_run[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) m_run[nt][0] = m_run[nt][1] = -INFINITY, l_run[nt][0] = l_run[nt][1] = 0.f;
-    const float c = a.scale_log2;
     uint32_t phase = 0;  // bit s: parity of stage s's next completion
     bool failed = false;
 
     int issued = 0;
-    for (; issued < count && issued < kAttnStages; ++issued) issue(issued);
+    for (; issued < count && issued < kStages; ++issued) issue(issued);
 
     for (int n = 0; n < issued; ++n) {
-        const int st = n % kAttnStages;
+        const int st = n % kStages;
         bool ready = false;
         if ((live >> st) & 1u) {
             uint64_t *bar = &bars[warp][st];
@@ -342,13 +449,33 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             float sc[NT][4], s2[NT][4];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = s2[nt][0] = s2[nt][1] = s2[nt][2] = s2[nt][3] = 0.f;
+            if constexpr (FP8) {
 #pragma unroll
-            for (int ks = 0; ks < D / 16; ++ks) {
-                uint32_t r[4];
-                ldsm_x4(r, kb + koff[ks & 3] + (ks >> 2) * kBoxBytes);
+                for (int pp = 0; pp < D / 32; ++pp) {
+                    // r0/r1: tokens g, g+8, dims 32pp + 4j..+3; r2/r3: the
+                    // next 16 dims. Low code pair -> k 2j, 2j+1; high -> 2j+8, 2j+9.
+                    uint32_t r[4];
+                    ldsm_x4(r, kb + koff[pp % kOffs] + (pp / kOffs) * G::kBoxBytes);
+                    uint32_t ae[4], ao[4];
+                    e4m3x4_to_f16x2x2(r[0], ae[0], ae[2]);
+                    e4m3x4_to_f16x2x2(r[1], ae[1], ae[3]);
+                    e4m3x4_to_f16x2x2(r[2], ao[0], ao[2]);
+                    e4m3x4_to_f16x2x2(r[3], ao[1], ao[3]);
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-                    mma16816<T>((ks & 1) ? s2[nt] : sc[nt], r, qb[nt][ks][0], qb[nt][ks][1]);
+                    for (int nt = 0; nt < NT; ++nt) {
+                        mma16816<C>(sc[nt], ae, qb[nt][2 * pp][0], qb[nt][2 * pp][1]);
+                        mma16816<C>(s2[nt], ao, qb[nt][2 * pp + 1][0], qb[nt][2 * pp + 1][1]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ++ks) {
+                    uint32_t r[4];
+                    ldsm_x4(r, kb + koff[ks & 3] + (ks >> 2) * G::kBoxBytes);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+                        mma16816<C>((ks & 1) ? s2[nt] : sc[nt], r, qb[nt][ks][0], qb[nt][ks][1]);
+                }
             }
             const int g = lane >> 2;
 #pragma unroll
@@ -365,10 +492,11 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                     if (g + 8 >= valid) sc[nt][2] = sc[nt][3] = -INFINITY;
                 }
                 unsigned char *vb = ring + st * G::kStageBytes + G::kTileBytes;
-                for (int i = lane; i < (kTok - valid) * G::kHalves * 8; i += 32) {
-                    const int r = valid + i / (G::kHalves * 8), cc = i % (G::kHalves * 8);
-                    *reinterpret_cast<uint4 *>(vb + (cc >> 3) * kBoxBytes + r * 128 + (cc & 7) * 16) =
-                        make_uint4(0, 0, 0, 0);
+                constexpr int kChunks = G::kBoxRow / 16;  // per row and box
+                for (int i = lane; i < (kTok - valid) * G::kBoxes * kChunks; i += 32) {
+                    const int r = valid + i / (G::kBoxes * kChunks), cc = i % (G::kBoxes * kChunks);
+                    *reinterpret_cast<uint4 *>(vb + (cc / kChunks) * G::kBoxBytes + r * G::kBoxRow +
+                                               (cc % kChunks) * 16) = make_uint4(0, 0, 0, 0);
                 }
                 __syncwarp();
             }
@@ -419,15 +547,37 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                     sc[nt][e] = ex2(fmaf(sc[nt][e], c, -m_run[nt][e & 1] * c));
                     l_run[nt][e & 1] += sc[nt][e];
                 }
-                pb[nt][0] = movmatrix_trans(pack2<T>(sc[nt][0], sc[nt][1]));
-                pb[nt][1] = movmatrix_trans(pack2<T>(sc[nt][2], sc[nt][3]));
+                pb[nt][0] = movmatrix_trans(pack2<C>(sc[nt][0], sc[nt][1]));
+                pb[nt][1] = movmatrix_trans(pack2<C>(sc[nt][2], sc[nt][3]));
             }
+            if constexpr (FP8) {
 #pragma unroll
-            for (int mt = 0; mt < D / 16; ++mt) {
-                uint32_t r[4];
-                ldsm_x4_trans(r, kb + voff[mt & 3] + (mt >> 2) * kBoxBytes);
+                for (int qq = 0; qq < D / 32; ++qq) {
+                    // Transposed b16 pairs: lane (g, j) holds tokens 2j, 2j+1
+                    // (+8 in r1/r3) at dims 2g, 2g+1 of chunk 2qq (r0/r1) and
+                    // 2qq+1 (r2/r3). Regrouped by dim, each pair of tokens is
+                    // one f16x2: row g of the m-tile is dim 2g, row g+8 is 2g+1.
+                    uint32_t r[4];
+                    ldsm_x4_trans(r, kb + voff[qq % kOffs] + (qq / kOffs) * G::kBoxBytes);
+                    uint32_t va[4], vb2[4];
+                    e4m3x4_to_f16x2x2(__byte_perm(r[0], 0, 0x3120), va[0], va[1]);
+                    e4m3x4_to_f16x2x2(__byte_perm(r[1], 0, 0x3120), va[2], va[3]);
+                    e4m3x4_to_f16x2x2(__byte_perm(r[2], 0, 0x3120), vb2[0], vb2[1]);
+                    e4m3x4_to_f16x2x2(__byte_perm(r[3], 0, 0x3120), vb2[2], vb2[3]);
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) mma16816<T>(o[nt][mt], r, pb[nt][0], pb[nt][1]);
+                    for (int nt = 0; nt < NT; ++nt) {
+                        mma16816<C>(o[nt][2 * qq], va, pb[nt][0], pb[nt][1]);
+                        mma16816<C>(o[nt][2 * qq + 1], vb2, pb[nt][0], pb[nt][1]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int mt = 0; mt < D / 16; ++mt) {
+                    uint32_t r[4];
+                    ldsm_x4_trans(r, kb + voff[mt & 3] + (mt >> 2) * G::kBoxBytes);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) mma16816<C>(o[nt][mt], r, pb[nt][0], pb[nt][1]);
+                }
             }
         }
         __syncwarp();
@@ -455,7 +605,8 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         for (int mt = 0; mt < D / 16; ++mt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int row = nt * 8 + (lane & 3) * 2 + (e & 1), d = mt * 16 + (lane >> 2) + (e >> 1) * 8;
+                const int row = nt * 8 + (lane & 3) * 2 + (e & 1);
+                const int d = FP8 ? mt * 16 + (lane >> 2) * 2 + (e >> 1) : mt * 16 + (lane >> 2) + (e >> 1) * 8;
                 om[(warp * 16 + row) * D + d] = o[nt][mt][e];
             }
     if (lane < 4) {
@@ -484,7 +635,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 acc += om[(w * 16 + row) * D + d] * f;
             }
         }
-        const float val = (L > 0.f && !failed) ? acc / L : 0.f;
+        const float val = (L > 0.f && !failed) ? acc / L * v_scale : 0.f;
         const float lse2 = (L > 0.f && !failed) ? M + log2f(L) : -INFINITY;
         const long long qh = (long long)kvh * a.group + row;
         const long long sq = (long long)seq * a.num_q_heads + qh;
@@ -542,10 +693,10 @@ paged_attention_combine_kernel(const AttnLaunch a) {
     }
 }
 
-template <typename T, int D>
+template <typename T, int D, bool FP8>
 cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t st) {
-    using G = AttnGeom<D>;
-    auto kern = a.group <= 8 ? paged_attention_kernel<T, D, 1> : paged_attention_kernel<T, D, 2>;
+    using G = AttnGeom<D, FP8>;
+    auto kern = a.group <= 8 ? paged_attention_kernel<T, D, 1, FP8> : paged_attention_kernel<T, D, 2, FP8>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)a.num_splits, (unsigned)a.kv_heads, (unsigned)a.num_seqs);
@@ -564,12 +715,12 @@ cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t
     return e;
 }
 
-template <typename T>
+template <typename T, bool FP8>
 cudaError_t launch_t(const AttnLaunch &a, const CUtensorMap *maps, int head_dim, cudaStream_t st) {
     switch (head_dim) {
-        case 64: return launch_td<T, 64>(a, maps, st);
-        case 128: return launch_td<T, 128>(a, maps, st);
-        case 256: return launch_td<T, 256>(a, maps, st);
+        case 64: return launch_td<T, 64, FP8>(a, maps, st);
+        case 128: return launch_td<T, 128, FP8>(a, maps, st);
+        case 256: return launch_td<T, 256, FP8>(a, maps, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -577,25 +728,32 @@ cudaError_t launch_t(const AttnLaunch &a, const CUtensorMap *maps, int head_dim,
 }  // namespace
 
 cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long long entry_elems,
-                                 long long rows, void *tmaps_out) {
+                                 long long rows, int head_dim, void *tmaps_out) {
     void *fn = nullptr;
     cudaDriverEntryPointQueryResult q{};
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
     if (e != cudaSuccess) return e;
     if (!fn || q != cudaDriverEntryPointSuccess) return cudaErrorNotSupported;
     auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    const CUtensorMapDataType t =
-        dtype == DType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    // The plane as [rows][entry] elements; a box is 16 rows x 64 elements (128 bytes).
+    const bool fp8 = dtype == DType::FP8_E4M3;
+    const CUtensorMapDataType t = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                  : dtype == DType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const int eb = fp8 ? 1 : 2;
+    // The plane as [rows][entry] elements; a box is 16 rows x 128 bytes
+    // (64 bf16/f16 or 128 E4M3 elements), or the 64 bytes of a 64-dim fp8
+    // head with the 64-byte swizzle (AttnGeom::chunk_at).
+    const int box_bytes = std::min(head_dim * eb, 128);
     const cuuint64_t dims[2] = {(cuuint64_t)entry_elems, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)entry_elems * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)kTok};
+    const cuuint64_t strides[1] = {(cuuint64_t)entry_elems * eb};
+    const cuuint32_t box[2] = {(cuuint32_t)(box_bytes / eb), (cuuint32_t)kTok};
     const cuuint32_t elem_strides[2] = {1, 1};
+    const CUtensorMapSwizzle swz = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUtensorMap *maps = static_cast<CUtensorMap *>(tmaps_out);
     void *planes[2] = {k_plane, v_plane};
     for (int i = 0; i < 2; ++i) {
         const CUresult r = encode(&maps[i], t, 2, planes[i], dims, strides, box, elem_strides,
-                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
@@ -614,13 +772,19 @@ int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_
     return std::max(1, (max_blocks + p - 1) / p);
 }
 
-cudaError_t launch_paged_attention(const AttnLaunch &a, const void *tmaps, DType dtype, int head_dim,
-                                   cudaStream_t st) {
+cudaError_t launch_paged_attention(const AttnLaunch &a, const void *tmaps, DType pool, DType query,
+                                   int head_dim, cudaStream_t st) {
     if (a.num_seqs <= 0 || a.kv_heads <= 0) return cudaSuccess;
     const CUtensorMap *maps = static_cast<const CUtensorMap *>(tmaps);
-    switch (dtype) {
-        case DType::BF16: return launch_t<__nv_bfloat16>(a, maps, head_dim, st);
-        case DType::F16: return launch_t<__half>(a, maps, head_dim, st);
+    if (pool == DType::FP8_E4M3) {
+        if (query == DType::BF16) return launch_t<__nv_bfloat16, true>(a, maps, head_dim, st);
+        if (query == DType::F16) return launch_t<__half, true>(a, maps, head_dim, st);
+        return cudaErrorInvalidValue;
+    }
+    if (query != pool) return cudaErrorInvalidValue;
+    switch (pool) {
+        case DType::BF16: return launch_t<__nv_bfloat16, false>(a, maps, head_dim, st);
+        case DType::F16: return launch_t<__half, false>(a, maps, head_dim, st);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -193,7 +193,9 @@ Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int s
         const size_t n = cfg.num_layers * cfg.num_kv_heads;
         b->k_scale_.assign(n, 1.0f);
         b->v_scale_.assign(n, 1.0f);
-        if ((e = cudaMalloc(&b->d_inv_, 2 * std::max<size_t>(n, 1) * sizeof(float))) != cudaSuccess)
+        // [k_inv][v_inv][k_scale][v_scale]: inverses for the quantising
+        // writes, scales for attention's dequantisation.
+        if ((e = cudaMalloc(&b->d_inv_, 4 * std::max<size_t>(n, 1) * sizeof(float))) != cudaSuccess)
             return device_error("allocating fp8 scales", e);
         Status st = b->upload_inv_scales();
         if (!st.ok()) return st;
@@ -459,10 +461,12 @@ Status B200Backend::fp8_source_error() const {
 
 Status B200Backend::upload_inv_scales() {
     const size_t n = k_scale_.size(), stride = std::max<size_t>(n, 1);
-    std::vector<float> inv(2 * stride, 1.0f);
+    std::vector<float> inv(4 * stride, 1.0f);
     for (size_t i = 0; i < n; ++i) {
         inv[i] = 1.0f / k_scale_[i];  // IEEE f32 division, rounded to nearest even
         inv[stride + i] = 1.0f / v_scale_[i];
+        inv[2 * stride + i] = k_scale_[i];
+        inv[3 * stride + i] = v_scale_[i];
     }
     DeviceGuard g(device_);
     cudaError_t e;
@@ -853,7 +857,7 @@ Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_s
 
 // Decode attention over one layer (no counterpart in the reference: the
 // trait leaves paged_attention for later, crates/paged-kv-core/src/backend.rs:18-22).
-Status B200Backend::paged_attention_dev(int64_t layer, const void *q, int64_t q_seq_stride,
+Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType query, int64_t q_seq_stride,
                                         int64_t num_seqs, int64_t num_q_heads,
                                         const int32_t *tables, int64_t table_stride,
                                         const int32_t *ctx, int64_t max_ctx, float softmax_scale,
@@ -861,8 +865,14 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, int64_t q_
     if (layer < 0 || (uint64_t)layer >= cfg_.num_layers)
         return error(PKV_ERR_INVALID_LAYER, layer, (int64_t)cfg_.num_layers,
                      msg_layer((uint64_t)layer, cfg_.num_layers));
-    if (dtype_ != DType::BF16 && dtype_ != DType::F16)
-        return error(PKV_ERR_DEVICE, 0, 0, "paged attention reads bf16 or f16 pools");
+    if (dtype_ == DType::FP8_E4M3) {
+        if (query != DType::BF16 && query != DType::F16)
+            return error(PKV_ERR_DEVICE, 0, 0, "attention over an fp8 pool takes bf16 or f16 queries");
+    } else if (dtype_ != DType::BF16 && dtype_ != DType::F16) {
+        return error(PKV_ERR_DEVICE, 0, 0, "paged attention reads bf16, f16 or fp8 (E4M3) pools");
+    } else if (query != dtype_) {
+        return error(PKV_ERR_DEVICE, 0, 0, "queries must have the pool dtype (bf16 or f16)");
+    }
     if (cfg_.block_size != 16)
         return error(PKV_ERR_DEVICE, 0, 0, "paged attention needs block_size 16");
     const uint64_t hd = cfg_.head_dim;
@@ -898,7 +908,7 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, int64_t q_
     cudaError_t e;
     if (!tmaps_ready_) {
         if ((e = make_attention_tmaps(k_plane_, v_plane_, dtype_, (long long)shard_entry_, rows,
-                                      tmaps_)) != cudaSuccess)
+                                      (int)hd, tmaps_)) != cudaSuccess)
             return device_error("building the attention tensor maps", e);
         tmaps_ready_ = true;
     }
@@ -919,6 +929,12 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, int64_t q_
     a.max_ctx = (int)max_ctx;
     a.num_splits = attention_splits((long long)num_seqs * kv, (int)max_ctx, sms_, &a.blocks_per_split);
     a.scale_log2 = softmax_scale * 1.4426950408889634f;
+    if (dtype_ == DType::FP8_E4M3) {
+        const long long stride = std::max<long long>((long long)(cfg_.num_layers * cfg_.num_kv_heads), 1);
+        a.k_scale = d_inv_ + 2 * stride;
+        a.v_scale = d_inv_ + 3 * stride;
+        a.scale_row = layer * (long long)cfg_.num_kv_heads + (long long)(elem_offset() / hd);
+    }
     a.err = d_err_;
     if (a.num_splits > 1) {
         const size_t parts = (size_t)num_seqs * num_q_heads * a.num_splits;
@@ -937,7 +953,7 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, int64_t q_
         a.part_o = d_attn_ws_;
         a.part_lse = d_attn_ws_ + parts * hd;
     }
-    return check("paged_attention", launch_paged_attention(a, tmaps_, dtype_, (int)hd, st));
+    return check("paged_attention", launch_paged_attention(a, tmaps_, dtype_, query, (int)hd, st));
 }
 
 Status B200Backend::digest(uint64_t *k, uint64_t *v, cudaStream_t st) {

@@ -63,7 +63,9 @@ class B200Backend {
     Status zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t s);
     Status set_copy_engine(int engine);
     Status set_kv_scales(const float *k_scales, const float *v_scales, uint64_t count);
-    Status paged_attention_dev(int64_t layer, const void *q, int64_t q_seq_stride,
+    // query: the type of q and out; the pool dtype for bf16/f16 pools, bf16
+    // or f16 over an fp8 pool.
+    Status paged_attention_dev(int64_t layer, const void *q, DType query, int64_t q_seq_stride,
                                int64_t num_seqs, int64_t num_q_heads, const int32_t *tables,
                                int64_t table_stride, const int32_t *ctx, int64_t max_ctx,
                                float softmax_scale, void *out, float *lse, cudaStream_t s);

@@ -193,10 +193,25 @@ int pkv_paged_attention_dev(pkv_backend *b, int64_t layer, const void *q, int64_
                             void *stream) {
     if (!b) return null_handle();
     return guarded([&] {
-        return b->impl->paged_attention_dev(layer, q, q_seq_stride, num_seqs, num_q_heads,
-                                            block_tables, table_stride, context_lens,
+        return b->impl->paged_attention_dev(layer, q, b->impl->dtype(), q_seq_stride, num_seqs,
+                                            num_q_heads, block_tables, table_stride, context_lens,
                                             max_context_len, softmax_scale, out, lse,
                                             as_stream(stream));
+    });
+}
+
+int pkv_paged_attention_typed_dev(pkv_backend *b, int64_t layer, const void *q, int query_dtype,
+                                  int64_t q_seq_stride, int64_t num_seqs, int64_t num_q_heads,
+                                  const int32_t *block_tables, int64_t table_stride,
+                                  const int32_t *context_lens, int64_t max_context_len,
+                                  float softmax_scale, void *out, float *lse, void *stream) {
+    if (!b) return null_handle();
+    if (!valid_dtype(query_dtype)) return bad_dtype();
+    return guarded([&] {
+        return b->impl->paged_attention_dev(layer, q, static_cast<pkv::DType>(query_dtype),
+                                            q_seq_stride, num_seqs, num_q_heads, block_tables,
+                                            table_stride, context_lens, max_context_len,
+                                            softmax_scale, out, lse, as_stream(stream));
     });
 }
 

@@ -178,6 +178,11 @@ struct AttnLaunch {
     float scale_log2;          // softmax scale * log2(e)
     float *part_o;             // [num_seqs][num_q_heads][num_splits][head_dim] when num_splits > 1
     float *part_lse;           // [num_seqs][num_q_heads][num_splits], base-2
+    // fp8 pools: dequantisation scales [num_layers][num_kv_heads] (device
+    // memory) and the index of this layer's first kv head held here.
+    const float *k_scale = nullptr;
+    const float *v_scale = nullptr;
+    long long scale_row = 0;
     DevError *err;
 };
 
@@ -201,9 +206,12 @@ cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t 
 // Paged decode attention (pkv_attention.cu). `tmaps` points at two
 // CUtensorMap objects (K plane, V plane) built by make_attention_tmaps.
 cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long long entry_elems,
-                                 long long rows, void *tmaps_out /* 2 x 128 bytes, 64-aligned */);
+                                 long long rows, int head_dim,
+                                 void *tmaps_out /* 2 x 128 bytes, 64-aligned */);
 int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split);
-cudaError_t launch_paged_attention(const AttnLaunch &a, const void *tmaps, DType dtype,
+// pool: the pool dtype; query: the type of q and out (the pool dtype for
+// bf16/f16 pools; bf16 or f16 over an fp8 pool).
+cudaError_t launch_paged_attention(const AttnLaunch &a, const void *tmaps, DType pool, DType query,
                                    int head_dim, cudaStream_t s);
 
 // fp8 (E4M3) pools (pkv_fp8.cu): quantising scatter, fused slot resolution +

@@ -68,6 +68,8 @@ _PROTOS = {
     "pkv_set_kv_scales": (_I, [_P, _P, _P, _U64]),
     "pkv_paged_attention_dev": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, C.c_float,
                                      _P, _P, _P]),
+    "pkv_paged_attention_typed_dev": (_I, [_P, _I64, _P, _I, _I64, _I64, _I64, _P, _I64, _P, _I64,
+                                           C.c_float, _P, _P, _P]),
     "pkv_resolve_slots_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P]),
     "pkv_resolve_and_cache_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P, _P,
                                        _I64, _I64, _I, _P]),
