@@ -942,10 +942,10 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType quer
         if (need > d_attn_ws_bytes_) {
             // The old workspace may still be read by attention work in flight.
             if ((e = cudaDeviceSynchronize()) != cudaSuccess) return device_error("cudaDeviceSynchronize", e);
+            const size_t want = std::max(need, d_attn_ws_bytes_ + d_attn_ws_bytes_ / 2);
             if (d_attn_ws_) cudaFree(d_attn_ws_);
             d_attn_ws_ = nullptr;
             d_attn_ws_bytes_ = 0;
-            const size_t want = std::max(need, d_attn_ws_bytes_ + d_attn_ws_bytes_ / 2);
             if ((e = cudaMalloc(&d_attn_ws_, want)) != cudaSuccess)
                 return device_error("allocating the attention workspace", e);
             d_attn_ws_bytes_ = want;
