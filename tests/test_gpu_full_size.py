@@ -13,7 +13,8 @@ the smaller cases does not fit a CPU at these sizes):
   updated by plain tensor indexing (cpu.rs:131-160 semantics).
 
 Geometry: Qwen2-7B KV heads (28 layers, 4 KV heads x 128, bf16, block size
-16) over a 32,768-block pool (30 GiB), as the benchmark configurations.
+16) over a 32,768-block pool (30 GiB), as the benchmark configurations; and
+config 5's 70B-like geometry over its 150 GB single-GPU pool.
 """
 
 import numpy as np
@@ -28,10 +29,10 @@ pytestmark = pytest.mark.gpu
 GEOM = dict(num_blocks=32768, block_size=16, num_kv_heads=4, head_dim=128, num_layers=28)
 
 
-def _fused_step_holds_its_properties(cuda, batch, pool_dtype):
+def _fused_step_holds_its_properties(cuda, batch, pool_dtype, cfg=None):
     import torch
 
-    cfg = CacheConfig(dtype_bytes=1 if pool_dtype == "fp8_e4m3" else 2, **GEOM)
+    cfg = cfg or CacheConfig(dtype_bytes=1 if pool_dtype == "fp8_e4m3" else 2, **GEOM)
     b = B200Backend(cfg, dtype=pool_dtype)
     if pool_dtype == "fp8_e4m3":
         st = Stream(7)
@@ -125,3 +126,18 @@ def test_config4_copy_and_zero_full_size(cuda, engine):
     del want, planes
     b.close()
     torch.cuda.empty_cache()
+
+
+def test_config5_geometry_full_pool(cuda):
+    """Config 5 on one GPU: 80 layers, 8 KV heads x 128, bf16, the 150 GB pool
+    (28,610 blocks: 3.75e10 elements per plane, far past 2^31). One step of a
+    16,384-token chunk of prompts (log-uniform 64..8192) written through the
+    fused kernel into blocks drawn from the whole pool."""
+    import torch
+
+    cfg = CacheConfig(num_blocks=28610, block_size=16, num_kv_heads=8, head_dim=128,
+                      num_layers=80, dtype_bytes=2)
+    torch.cuda.empty_cache()  # the pool and its rows need 155 GB of the 183
+    batch = prefill_chunk(seed=5, num_prompts=40, lo=64, hi=8192, budget=16384, cfg=cfg)
+    assert batch.tables.max() > cfg.num_blocks * 3 // 4  # reaches the top of the pool
+    _fused_step_holds_its_properties(cuda, batch, "bf16", cfg=cfg)
