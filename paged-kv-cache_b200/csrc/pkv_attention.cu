@@ -379,7 +379,8 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     // This warp's block ids, one per lane (count <= 32: splits hold at most
     // 128 blocks), read once so that no table load sits in the block loop.
     const int my_blk = lane < count ? __ldg(table + first + kAttnWarps * lane) : -1;
-    uint32_t live = 0;  // bit s: stage s holds a block in flight (block id inside the pool)
+    uint32_t live = 0;   // bit s: stage s holds a block in flight (block id inside the pool)
+    uint32_t dirty = 0;  // bit s: stage s's V rows were zeroed by generic stores
     auto issue = [&](int i) {
         const int st = i % kStages;
         const int blk = __shfl_sync(0xffffffffu, my_blk, i);
@@ -389,12 +390,16 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             return;
         }
         live |= 1u << st;
+        const bool fence = (dirty >> st) & 1u;
+        dirty &= ~(1u << st);
         if (lane == 0) {
             unsigned char *buf = ring + st * G::kStageBytes;
             uint64_t *bar = &bars[warp][st];
-            // Earlier generic-proxy reads and writes of this buffer come
-            // before the async-proxy writes of the copy.
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            // The tail of a sequence zeroes V rows with generic stores; those
+            // come before the async-proxy writes of the next copy into the
+            // buffer. (Its ldmatrix reads have completed: their values fed
+            // the mma that issued before this, and the warp synchronised.)
+            if (fence) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_expect_tx(bar, (uint32_t)G::kStageBytes);
             const int y = a.layer_row0 + blk * kTok;
 #pragma unroll
@@ -498,6 +503,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                     *reinterpret_cast<uint4 *>(vb + (cc / kChunks) * G::kBoxBytes + r * G::kBoxRow +
                                                (cc % kChunks) * 16) = make_uint4(0, 0, 0, 0);
                 }
+                dirty |= 1u << st;
                 __syncwarp();
             }
             // Online softmax per query head (a column of S^T, spread over the
