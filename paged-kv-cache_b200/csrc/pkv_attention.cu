@@ -50,6 +50,14 @@ namespace {
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxStages = 6;
+// Pool blocks per split, at most: a CTA has a fixed cost (queries, barrier
+// set-up, the first copies' round trip, the warp merge), so long splits pay
+// best. 128 is the most the per-warp block-id prefetch holds (32 a warp);
+// measured on the config-2 batch: 16 / 32 / 64 / 128 blocks gave 0.65 /
+// 0.82 / 0.89 / 0.90 of peak.
+#ifndef PKV_ATTN_SPLIT_BLOCKS
+#define PKV_ATTN_SPLIT_BLOCKS 128
+#endif
 constexpr int kTok = 16;                 // tokens per pool block
 constexpr int kDeviceCode = 9;           // PKV_ERR_DEVICE
 constexpr long long kAttnWaitCycles = 4000000000ll;  // about 2 s at 2 GHz
@@ -60,7 +68,7 @@ constexpr long long kAttnWaitCycles = 4000000000ll;  // about 2 s at 2 GHz
 // rows of a 64-dim fp8 head: c ^ ((r / 2) % 4)). fp8 tiles are half as big,
 // so three stages a warp leave room for four CTAs per SM: the same bytes in
 // flight as two CTAs of bf16 tiles, and 16 warps to hide the conversions.
-template <int D, bool FP8>
+template <int D, bool FP8, int STAGES>
 struct AttnGeom {
     static constexpr int kElemBytes = FP8 ? 1 : 2;
     static constexpr int kRowBytes = D * kElemBytes;                       // one head's row
@@ -69,7 +77,7 @@ struct AttnGeom {
     static constexpr int kBoxes = kRowBytes / kBoxRow;                     // boxes per tile
     static constexpr int kBoxBytes = kTok * kBoxRow;
     static constexpr int kTileBytes = kBoxes * kBoxBytes;                  // 16 tokens x D elements
-    static constexpr int kStages = 3;
+    static constexpr int kStages = STAGES;
     static constexpr int kStageBytes = 2 * kTileBytes;                     // K tile, then V tile
     static constexpr int kRingBytes = kStages * kStageBytes;
     static constexpr int kQPitch = (D + 8) * 2;               // padded: conflict-free ldmatrix
@@ -85,6 +93,19 @@ struct AttnGeom {
         return kBoxRow == 128 ? r * 128 + ((c ^ (r & 7)) << 4) : r * kBoxRow + ((c ^ ((r >> 1) & 3)) << 4);
     }
 };
+
+// Stages per warp and CTAs per SM of each form: the bytes in flight per SM
+// stay 4 warps x 3 stages x 2 CTAs of bf16/f16 tiles, spread over as many
+// CTAs as registers allow, so that one CTA's set-up and merge overlap the
+// others' streaming.
+template <int D, bool FP8>
+__host__ __device__ constexpr int attn_stages(int nt) {
+    return (D <= 128 && nt == 1 && !FP8) ? 2 : 3;
+}
+template <int D, bool FP8>
+__host__ __device__ constexpr int attn_min_ctas(int nt) {
+    return D > 128 ? 2 : FP8 ? (nt == 1 ? 4 : 3) : (nt == 1 ? 3 : 2);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -231,10 +252,10 @@ __device__ __forceinline__ int checked_ctx(const AttnLaunch &a, int seq, bool re
 // runs in f16 (queries too, scaled by a power of two into f16 range), with
 // the K scale folded into the softmax scale and the V scale into the output.
 template <typename T, int D, int NT, bool FP8>
-__global__ void __launch_bounds__(kAttnThreads, (FP8 && D <= 128) ? (NT == 1 ? 4 : 3) : 2)
+__global__ void __launch_bounds__(kAttnThreads, attn_min_ctas<D, FP8>(NT))
 paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                        const AttnLaunch a) {
-    using G = AttnGeom<D, FP8>;
+    using G = AttnGeom<D, FP8, attn_stages<D, FP8>(NT)>;
     using C = std::conditional_t<FP8, __half, T>;  // tensor-core operand type
     constexpr int kStages = G::kStages;
     extern __shared__ unsigned char smem_raw[];
@@ -699,15 +720,22 @@ paged_attention_combine_kernel(const AttnLaunch a) {
     }
 }
 
-template <typename T, int D, bool FP8>
-cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t st) {
-    using G = AttnGeom<D, FP8>;
-    auto kern = a.group <= 8 ? paged_attention_kernel<T, D, 1, FP8> : paged_attention_kernel<T, D, 2, FP8>;
+template <typename T, int D, int NT, bool FP8>
+cudaError_t launch_main(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t st) {
+    using G = AttnGeom<D, FP8, attn_stages<D, FP8>(NT)>;
+    auto kern = paged_attention_kernel<T, D, NT, FP8>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)a.num_splits, (unsigned)a.kv_heads, (unsigned)a.num_seqs);
     kern<<<grid, kAttnThreads, G::kSmem, st>>>(maps[0], maps[1], a);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+template <typename T, int D, bool FP8>
+cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t st) {
+    cudaError_t e = a.group <= 8 ? launch_main<T, D, 1, FP8>(a, maps, st)
+                                 : launch_main<T, D, 2, FP8>(a, maps, st);
+    if (e != cudaSuccess) return e;
     if (a.num_splits > 1) {
         const size_t smem = (size_t)a.num_q_heads * a.num_splits * sizeof(float);
         if (smem > 227 * 1024) return cudaErrorInvalidValue;
@@ -769,10 +797,10 @@ cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long
 
 int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split) {
     const int max_blocks = (max_ctx + kTok - 1) / kTok;
-    // At least one block per warp per split, at most 64 (1,024 tokens);
+    // At least one block per warp per split, at most PKV_ATTN_SPLIT_BLOCKS;
     // fewer blocks per split while the (sequence, kv head) pairs alone cannot
     // fill two CTAs per SM.
-    int p = 64;
+    int p = PKV_ATTN_SPLIT_BLOCKS;
     while (p > kAttnWarps && num_pairs * ((max_blocks + p - 1) / p) < 2LL * sms) p /= 2;
     *blocks_per_split = p;
     return std::max(1, (max_blocks + p - 1) / p);
