@@ -272,6 +272,9 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     const int nblk = (ctx + kTok - 1) / kTok;
     const int b0 = split * a.blocks_per_split;
     const int b1 = min(nblk, b0 + a.blocks_per_split);
+    // The combine kernel (launched as a programmatic dependent of this grid)
+    // may be scheduled from here on; it waits for this grid's completion.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (split > 0 && b0 >= b1) return;  // beyond this sequence's splits: the combine skips it
 
     // Query tile: row r < group is query head kvh * group + r; other rows zero.
@@ -683,6 +686,10 @@ template <typename T, int D>
 __global__ void __launch_bounds__(256)
 paged_attention_combine_kernel(const AttnLaunch a) {
     extern __shared__ float s_w[];  // [num_q_heads][num_splits]
+    // Launched as a programmatic dependent of the attention grid: its CTAs
+    // can take SM slots while the attention's last CTAs run, and wait here
+    // until that grid has completed and its partials are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int seq = blockIdx.x;
     const int ctx = checked_ctx(a, seq, false);
     const int nblk = (ctx + kTok - 1) / kTok;
@@ -743,8 +750,17 @@ cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t
             (e = cudaFuncSetAttribute(paged_attention_combine_kernel<T, D>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
             return e;
-        paged_attention_combine_kernel<T, D><<<(unsigned)a.num_seqs, 256, smem, st>>>(a);
-        e = cudaGetLastError();
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)a.num_seqs);
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, paged_attention_combine_kernel<T, D>, a);
     }
     return e;
 }
