@@ -74,11 +74,15 @@ def parse():
     p.add_argument("--profile-small", action="store_true",
                    help="an 8,192-token chunk over a 2,048-block pool and nothing else, "
                         "for ncu captures")
+    p.add_argument("--with-ops", action="store_true",
+                   help="with --profile-small: also the per-kernel timings (copy_blocks, "
+                        "zero_blocks, decode step) over the small pool")
     a = p.parse_args()
     a.chunk_tokens, a.chunk_prompts, a.chunk_blocks = CHUNK_TOKENS, CHUNK_PROMPTS, BLOCKS_PER_CHUNK
     if a.profile_small:
         a.chunk_tokens, a.chunk_prompts, a.chunk_blocks = 8192, 16, 2048
-        a.no_e2e = a.no_cpu = a.no_ops = True
+        a.no_e2e = a.no_cpu = True
+        a.no_ops = not a.with_ops
     return a
 
 
