@@ -180,13 +180,21 @@ __device__ __forceinline__ float ex2(float x) {
 
 // Four E4M3 codes (byte 0 first) as two f16 pairs: bytes 0, 1 -> lo (byte 0
 // in the low half), bytes 2, 3 -> hi. Exact: every E4M3 value is an f16 value.
+__device__ __forceinline__ uint32_t e4m3x2_lo_to_f16x2(uint32_t codes) {
+    uint32_t y;
+    asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\t}"
+        : "=r"(y) : "r"(codes));
+    return y;
+}
+__device__ __forceinline__ uint32_t e4m3x2_hi_to_f16x2(uint32_t codes) {
+    uint32_t y;
+    asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, b;\n\t}"
+        : "=r"(y) : "r"(codes));
+    return y;
+}
 __device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t codes, uint32_t &lo, uint32_t &hi) {
-    asm("{\n\t.reg .b16 a, b;\n\t"
-        "mov.b32 {a, b}, %2;\n\t"
-        "cvt.rn.f16x2.e4m3x2 %0, a;\n\t"
-        "cvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
-        : "=r"(lo), "=r"(hi)
-        : "r"(codes));
+    lo = e4m3x2_lo_to_f16x2(codes);
+    hi = e4m3x2_hi_to_f16x2(codes);
 }
 
 template <typename T>
@@ -405,8 +413,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     const int my_blk = lane < count ? __ldg(table + first + kAttnWarps * lane) : -1;
     uint32_t live = 0;   // bit s: stage s holds a block in flight (block id inside the pool)
     uint32_t dirty = 0;  // bit s: stage s's V rows were zeroed by generic stores
-    auto issue = [&](int i) {
-        const int st = i % kStages;
+    auto issue = [&](int i, int st) {  // st == i % kStages
         const int blk = __shfl_sync(0xffffffffu, my_blk, i);
         if (blk < 0 || blk >= a.num_blocks) {
             if (lane == 0) record_error(a.err, kInvalidBlock, seq);
@@ -437,24 +444,29 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     // O^T accumulators: o[nt][mt] is the m16n8 tile (dims 16mt.., query heads
     // 8nt..); this lane holds dims 16mt + g (+8) of heads 8nt + 2j (+1), with
     // g = lane / 4, j = lane % 4 (fp8: dims 16mt + 2g (+1), the order the V
-    // fragments arrive in). Running maxima (raw score units; the scale is
-    // positive) and sums per query head: [nt][hc] is head 8nt + 2j + hc.
+    // fragments arrive in). Reference points (base-2 units: a raw score
+    // times c) and sums per query head: [nt][hc] is head 8nt + 2j + hc.
     float o[NT][D / 16][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int mt = 0; mt < D / 16; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
-    float m_run[NT][2], l_run[NT][2];
+    float mc[NT][2], l_run[NT][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) m_run[nt][0] = m_run[nt][1] = -INFINITY, l_run[nt][0] = l_run[nt][1] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) mc[nt][0] = mc[nt][1] = -INFINITY, l_run[nt][0] = l_run[nt][1] = 0.f;
     uint32_t phase = 0;  // bit s: parity of stage s's next completion
     bool failed = false;
 
     int issued = 0;
-    for (; issued < count && issued < kStages; ++issued) issue(issued);
+#pragma unroll
+    for (int i = 0; i < kStages; ++i)
+        if (i < count) issue(issued++, i);
 
-    for (int n = 0; n < issued; ++n) {
-        const int st = n % kStages;
+    // Block n of this warp sits in stage n % kStages; the loop is unrolled
+    // by the stage count so that each stage's index, barrier, buffer and
+    // phase bit are constants. Block n + kStages, issued after block n is
+    // consumed, reuses block n's stage.
+    auto consume = [&](const int n, const int st) {
         bool ready = false;
         if ((live >> st) & 1u) {
             uint64_t *bar = &bars[warp][st];
@@ -531,39 +543,39 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 __syncwarp();
             }
             // Online softmax per query head (a column of S^T, spread over the
-            // 8 lanes with the same j) in base 2: p = 2^((s - m) * c). The
-            // reference point m moves only when a head's maximum exceeds it
-            // by more than 2^8 in weight, so most blocks skip the rescale;
-            // weights stay below 2^8, which f32 sums and bf16/f16 weights hold
-            // with the same relative precision as weights below 1.
-            float m_new[NT][2];
+            // 8 lanes with the same j) in base 2: p = 2^(s * c - m). The
+            // reference point m moves only when some score of the head
+            // exceeds it by more than 8 (2^8 in weight), so most blocks skip
+            // the rescale, and each lane tests only its own scores: the
+            // head's exact maximum (3 shuffles) is taken on the rare path
+            // alone. Weights stay below 2^8, which f32 sums and bf16/f16
+            // weights hold with the same relative precision as weights below 1.
             bool grew = false;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int hc = 0; hc < 2; ++hc) {
-                    float mx = fmaxf(sc[nt][hc], sc[nt][2 + hc]);
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    m_new[nt][hc] = fmaxf(m_run[nt][hc], mx);  // finite: token 0 is valid
-                    grew |= (m_new[nt][hc] - m_run[nt][hc]) * c > 8.0f;  // always on the first block
-                }
+                for (int hc = 0; hc < 2; ++hc)  // always on the first block (m = -inf)
+                    grew |= fmaf(fmaxf(sc[nt][hc], sc[nt][2 + hc]), c, -mc[nt][hc]) > 8.0f;
             if (__any_sync(0xffffffffu, grew)) {
                 // Move every head's reference point to its maximum: rescale
-                // its sum and output by 2^((m_old - m_new) * c).
+                // its sum and output by 2^(m_old - m_new).
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int hc = 0; hc < 2; ++hc) {
-                        const float corr = ex2((m_run[nt][hc] - m_new[nt][hc]) * c);
+                        float mx = fmaxf(sc[nt][hc], sc[nt][2 + hc]);
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                        const float m_new = fmaxf(mc[nt][hc], mx * c);  // finite: token 0 is valid
+                        const float corr = ex2(mc[nt][hc] - m_new);
                         l_run[nt][hc] *= corr;
 #pragma unroll
                         for (int mt = 0; mt < D / 16; ++mt) {
                             o[nt][mt][hc] *= corr;
                             o[nt][mt][2 + hc] *= corr;
                         }
-                        m_run[nt][hc] = m_new[nt][hc];
+                        mc[nt][hc] = m_new;
                     }
             }
             // P^T as the B operand of O^T = V^T . P^T: pack this lane's
@@ -574,7 +586,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    sc[nt][e] = ex2(fmaf(sc[nt][e], c, -m_run[nt][e & 1] * c));
+                    sc[nt][e] = ex2(fmaf(sc[nt][e], c, -mc[nt][e & 1]));
                     l_run[nt][e & 1] += sc[nt][e];
                 }
                 pb[nt][0] = movmatrix_trans(pack2<C>(sc[nt][0], sc[nt][1]));
@@ -611,7 +623,12 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             }
         }
         __syncwarp();
-        if (!failed && issued < count) issue(issued++);
+        if (!failed && issued < count) issue(issued++, st);
+    };
+    for (int n0 = 0; n0 < issued; n0 += kStages) {
+#pragma unroll
+        for (int st = 0; st < kStages; ++st)
+            if (n0 + st < issued) consume(n0 + st, st);
     }
 
     // Per-head sums over the 8 lanes (g = 0..7) that share a head.
@@ -645,7 +662,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
 #pragma unroll
             for (int hc = 0; hc < 2; ++hc) {
                 const int row = nt * 8 + lane * 2 + hc;
-                mm[warp * 16 + row] = m_run[nt][hc] * c;  // base-2 units, as the merge expects
+                mm[warp * 16 + row] = mc[nt][hc];  // base-2 units, as the merge expects
                 ll[warp * 16 + row] = l_run[nt][hc];
             }
     }
