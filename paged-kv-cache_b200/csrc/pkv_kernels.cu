@@ -290,9 +290,68 @@ resolve_slots_kernel(const int *__restrict__ tables, long long table_stride,
 // reshape_copy_kernel does. The vector-0 threads of layer chunk 0 also
 // publish the slot (when asked) so attention can use it.
 
-template <typename V, int UNROLL, int MIN_CTAS>
-__global__ void __launch_bounds__(kThreads, MIN_CTAS)
-resolve_cache_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
+// Moves item (t, vec)'s vector for layers [l0, l1) to slot s, UNROLL
+// layers' K and V loads in flight at a time; the first `have` layers' rows
+// are already in kr/vr.
+template <typename V, int UNROLL>
+__device__ __forceinline__ void move_item(const ResolveCacheLaunch &a, int nvec, int l0, int l1,
+                                          long long t, int vec, long long s, V (&kr)[UNROLL],
+                                          V (&vr)[UNROLL], int have) {
+    const long long entry_bytes = (long long)nvec * sizeof(V);
+    const long long pool_layer = a.slots_per_layer * entry_bytes;
+    const long long src_tok = a.src_token_stride_bytes, src_layer = a.src_layer_stride_bytes;
+    const long long col = (long long)vec * sizeof(V);
+    const char *ks = static_cast<const char *>(a.k) + t * src_tok + l0 * src_layer + col;
+    const char *vs = static_cast<const char *>(a.v) + t * src_tok + l0 * src_layer + col;
+    char *kd = static_cast<char *>(a.k_pool) + (a.first_layer + l0) * pool_layer + s * entry_bytes + col;
+    char *vd = static_cast<char *>(a.v_pool) + (a.first_layer + l0) * pool_layer + s * entry_bytes + col;
+    int l = l0;
+    if (have > 0) {
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u)
+            if (u < have) {
+                __stcs(reinterpret_cast<V *>(kd + u * pool_layer), kr[u]);
+                __stcs(reinterpret_cast<V *>(vd + u * pool_layer), vr[u]);
+            }
+        ks += have * src_layer;
+        vs += have * src_layer;
+        kd += have * pool_layer;
+        vd += have * pool_layer;
+        l += have;
+    }
+    for (; l + UNROLL <= l1; l += UNROLL) {
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            kr[u] = __ldcs(reinterpret_cast<const V *>(ks + u * src_layer));
+            vr[u] = __ldcs(reinterpret_cast<const V *>(vs + u * src_layer));
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            __stcs(reinterpret_cast<V *>(kd + u * pool_layer), kr[u]);
+            __stcs(reinterpret_cast<V *>(vd + u * pool_layer), vr[u]);
+        }
+        ks += UNROLL * src_layer;
+        vs += UNROLL * src_layer;
+        kd += UNROLL * pool_layer;
+        vd += UNROLL * pool_layer;
+    }
+    for (; l < l1; ++l) {
+        const V k1 = __ldcs(reinterpret_cast<const V *>(ks));
+        const V v1 = __ldcs(reinterpret_cast<const V *>(vs));
+        __stcs(reinterpret_cast<V *>(kd), k1);
+        __stcs(reinterpret_cast<V *>(vd), v1);
+        ks += src_layer;
+        vs += src_layer;
+        kd += pool_layer;
+        vd += pool_layer;
+    }
+}
+
+// The general step: scan new_lens, then resolve and move every item of the
+// grid-stride loop. Every thread of the CTA must call it.
+template <typename V, int UNROLL>
+__device__ __forceinline__ void resolve_cache_general(const ResolveCacheLaunch &a, int nvec,
+                                                      int layers_per_chunk) {
     extern __shared__ int s_cu[];
     __shared__ int s_warp[kThreads / 32];
     __shared__ int s_bad;
@@ -360,6 +419,82 @@ resolve_cache_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
             vd += pool_layer;
         }
     }
+}
+
+// The same, compiled on its own: the decode kernel's rarely taken fallback,
+// so that its registers do not weigh on the decode path.
+template <typename V, int UNROLL>
+__device__ __noinline__ void resolve_cache_general_call(ResolveCacheLaunch a, int nvec,
+                                                        int layers_per_chunk) {
+    resolve_cache_general<V, UNROLL>(a, nvec, layers_per_chunk);
+}
+
+template <typename V, int UNROLL, int MIN_CTAS>
+__global__ void __launch_bounds__(kThreads, MIN_CTAS)
+resolve_cache_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
+    resolve_cache_general<V, UNROLL>(a, nvec, layers_per_chunk);
+}
+
+// A decode step (one new token per sequence, num_tokens == num_seqs, one
+// work item per thread): token t is sequence t's token, at position
+// ctx_lens[t], so no scan is needed. Each thread issues its context length
+// and its rows' loads first, then the CTA checks with one barrier that every
+// new_lens is 1 (and every context non-negative); only the block-table load
+// and the stores remain after it. If the check fails, every CTA (they all
+// read the same lengths) takes the general path instead.
+template <typename V, int UNROLL>
+__global__ void __launch_bounds__(kThreads, 4)
+resolve_cache_decode_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
+    const long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool active = it < a.num_tokens * nvec;
+    const int l0 = blockIdx.y * layers_per_chunk;
+    const int l1 = min((int)a.num_layers, l0 + layers_per_chunk);
+    const int have = min(UNROLL, l1 - l0);
+    long long t = 0;
+    int vec = 0, pos = 0;
+    V kr[UNROLL], vr[UNROLL];
+    if (active) {
+        t = it / nvec;
+        vec = (int)(it - t * nvec);
+        pos = __ldg(a.ctx_lens + t);
+        const long long off = t * a.src_token_stride_bytes + l0 * a.src_layer_stride_bytes +
+                              (long long)vec * sizeof(V);
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u)
+            if (u < have) {
+                kr[u] = __ldcs(reinterpret_cast<const V *>(static_cast<const char *>(a.k) + off +
+                                                           u * a.src_layer_stride_bytes));
+                vr[u] = __ldcs(reinterpret_cast<const V *>(static_cast<const char *>(a.v) + off +
+                                                           u * a.src_layer_stride_bytes));
+            }
+    }
+    int ok = 1;
+    for (int q = threadIdx.x; q < a.num_seqs; q += kThreads)
+        ok &= (__ldg(a.new_lens + q) == 1) & (__ldg(a.ctx_lens + q) >= 0);
+    if (!__syncthreads_and(ok)) {
+        resolve_cache_general_call<V, UNROLL>(a, nvec, layers_per_chunk);
+        return;
+    }
+    if (blockIdx.x == 0 && blockIdx.y == 0)
+        for (int q = threadIdx.x; q <= a.num_seqs; q += kThreads) a.cu_seqlens[q] = q;
+    if (!active) return;
+    // BlockTable::slot_for_position (block_table.rs:97-101) of position pos.
+    const bool lead = vec == 0 && blockIdx.y == 0;
+    const long long lb = pos / a.block_size;
+    long long s = -1;
+    if (lb >= a.table_stride) {
+        if (lead) record_error(a.err, kSlotOutOfRange, t);
+    } else {
+        const long long blk = __ldg(a.tables + t * a.table_stride + lb);
+        if (blk < 0 || blk >= a.num_blocks) {
+            if (lead) record_error(a.err, kInvalidBlock, t);
+        } else {
+            s = blk * a.block_size + (pos - lb * a.block_size);
+        }
+    }
+    if (lead && a.slots_out) a.slots_out[t] = s;
+    if (s < 0) return;
+    move_item<V, UNROLL>(a, nvec, l0, l1, t, vec, s, kr, vr, have);
 }
 
 // ---- digest --------------------------------------------------------------------
@@ -676,7 +811,11 @@ cudaError_t resolve_cache_v(const ResolveCacheLaunch &a, long long entry_bytes, 
     // 80 registers a thread: measured on B200, 0.989 of the copy peak against
     // 0.974 at 4 CTAs per SM and 64 registers.
     const bool one_wave = (long long)grid.x * grid.y <= (long long)sms * 4;
-    auto kern = one_wave ? resolve_cache_kernel<V, 4, 4> : resolve_cache_kernel<V, 4, 3>;
+    // One new token per sequence with every item in the first pass of the
+    // grid: the decode form, which skips the scan when the lengths allow.
+    const bool decode = a.num_tokens == a.num_seqs && (long long)bx * kThreads >= items;
+    auto kern = decode ? resolve_cache_decode_kernel<V, 4>
+                : one_wave ? resolve_cache_kernel<V, 4, 4> : resolve_cache_kernel<V, 4, 3>;
     const size_t smem = (size_t)(a.num_seqs + 1) * sizeof(int);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -587,6 +587,70 @@ def test_fused_resolve_and_cache_equals_resolve_then_reshape(cuda, case):
         assert_pools_equal(fus, cpu)
 
 
+@pytest.mark.parametrize("case", ["ones", "mixed_lengths", "bad_block", "past_table",
+                                  "negative_ctx"])
+def test_decode_form_of_the_fused_step_matches_the_general_form(cuda, case):
+    """With one token per sequence (num_tokens == num_seqs) the fused step
+    takes its decode form: no length scan when every new_lens is 1, the
+    general scan otherwise (lengths such as [2, 0, 1, ...] that also sum to
+    the sequence count, or a negative context). Pools, cu_seqlens, slots and
+    the recorded error must equal resolve_slots + reshape_and_cache."""
+    import torch
+
+    cfg = CacheConfig(2048, 16, 2, 64, 5, 2)
+    e = cfg.entry_elems()
+    st = Stream(70)
+    batch = decode_batch(seed=None, num_seqs=96, max_ctx=300, cfg=cfg)
+    tables, ctx, new = batch.tables.copy(), batch.ctx.copy(), batch.new.copy()
+    if case == "mixed_lengths":
+        new[0], new[1] = 2, 0  # still 96 tokens for 96 sequences
+        need = -(-(ctx[0] + 2) // 16)
+        if tables[0, need - 1] < 0:
+            tables[0, need - 1] = int(np.setdiff1d(np.arange(cfg.num_blocks), tables)[0])
+    elif case == "bad_block":
+        q = 7
+        tables[q, int(ctx[q]) // 16] = cfg.num_blocks + 3
+    elif case == "past_table":
+        q = 11
+        ctx[q] = tables.shape[1] * 16  # its new token's block is past the table
+    elif case == "negative_ctx":
+        ctx[5] = -1
+    t = int(new.sum())
+    assert t == len(new)
+    kv = f32_to_bf16_bits(st.normal(2 * cfg.num_layers * t * e)).reshape(2, cfg.num_layers, t, e)
+    d_kv = torch.from_numpy(kv.view(np.int16)).view(torch.bfloat16).to(cuda)
+    tab, dctx, dnew = (torch.from_numpy(x).to(cuda) for x in (tables, ctx, new))
+    ref = B200Backend(cfg, dtype="bf16")
+    cu_ref = torch.full((len(new) + 1,), -5, dtype=torch.int32, device=cuda)
+    sl_ref = torch.full((t,), -9, dtype=torch.int64, device=cuda)
+    ref.resolve_slots(tab, dctx, dnew, t, cu_ref, sl_ref)
+    torch.cuda.synchronize()
+    err_ref = ref.device_error()
+    if case != "negative_ctx":
+        ref.reshape_and_cache(d_kv[0], d_kv[1], sl_ref)
+    fus = B200Backend(cfg, dtype="bf16")
+    cu = torch.full_like(cu_ref, -5)
+    sl = torch.full_like(sl_ref, -9)
+    fus.resolve_and_cache(tab, dctx, dnew, t, cu, d_kv[0], d_kv[1], slots_out=sl)
+    torch.cuda.synchronize()
+    err = fus.device_error()
+    if case in ("ones", "mixed_lengths"):
+        assert err is None and err_ref is None
+    else:
+        assert err is not None and err_ref is not None
+        assert type(err[0]) is type(err_ref[0]) and err[1] == err_ref[1]
+    if case == "negative_ctx":  # nothing is written; cu_seqlens is still published
+        assert torch.equal(cu, cu_ref)
+        for p_ in fus.planes():
+            assert int(torch.count_nonzero(p_)) == 0
+        return
+    assert torch.equal(cu, cu_ref)
+    assert torch.equal(sl, sl_ref)
+    assert ref.device_error() is None
+    for a, b in zip(fus.planes(), ref.planes()):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
 def test_fused_resolve_and_cache_flags_bad_tables_and_writes_nothing_for_them(cuda):
     import torch
 
