@@ -24,6 +24,12 @@
  * trait's mutating methods take &mut self). Host-buffer methods issue their
  * work on the handle's own blocking CUDA stream, which is ordered with the
  * legacy default stream; device entry points use the stream they are given.
+ * Per-handle device state is shared by the calls that use it: the device
+ * error word (all entry points) and the split workspace of
+ * pkv_paged_attention_dev. Calls on one handle that run concurrently on
+ * different streams share them too, so give one handle's device calls one
+ * stream (or order the streams) when the error word or attention's
+ * partial results must stay apart.
  */
 #ifndef PKV_B200_H
 #define PKV_B200_H
