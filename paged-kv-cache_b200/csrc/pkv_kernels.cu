@@ -807,15 +807,17 @@ cudaError_t resolve_cache_v(const ResolveCacheLaunch &a, long long entry_bytes, 
     long long bx = std::min<long long>((items + kThreads - 1) / kThreads, (long long)sms * 256);
     dim3 grid((unsigned)std::max<long long>(bx, 1), (unsigned)chunks);
     // A launch that fits one wave at 4 CTAs per SM (a decode step) keeps
-    // that residency. Larger ones (a prefill chunk) run at 3 CTAs per SM with
-    // 80 registers a thread: measured on B200, 0.989 of the copy peak against
-    // 0.974 at 4 CTAs per SM and 64 registers.
+    // that residency. Larger ones (a prefill chunk) run at 2 CTAs per SM with
+    // up to 128 registers a thread: fewer write streams in flight per SM.
+    // Measured on B200 (65,536-token chunk, alternating builds): 1.004 of the
+    // copy peak, against 0.989 at 3 CTAs per SM (80 registers) and 0.974 at 4
+    // (64 registers); 2 layers in flight instead of 4 at 2 CTAs per SM: 0.927.
     const bool one_wave = (long long)grid.x * grid.y <= (long long)sms * 4;
     // One new token per sequence with every item in the first pass of the
     // grid: the decode form, which skips the scan when the lengths allow.
     const bool decode = a.num_tokens == a.num_seqs && (long long)bx * kThreads >= items;
     auto kern = decode ? resolve_cache_decode_kernel<V, 4>
-                : one_wave ? resolve_cache_kernel<V, 4, 4> : resolve_cache_kernel<V, 4, 3>;
+                : one_wave ? resolve_cache_kernel<V, 4, 4> : resolve_cache_kernel<V, 4, 2>;
     const size_t smem = (size_t)(a.num_seqs + 1) * sizeof(int);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
