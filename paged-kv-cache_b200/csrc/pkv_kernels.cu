@@ -49,8 +49,8 @@ __device__ __forceinline__ __half from_f32<__half>(float f) { return __float2hal
 // Consecutive threads cover consecutive vectors of one entry, so every warp
 // reads and writes whole contiguous runs.
 
-template <typename V, int UNROLL>
-__global__ void __launch_bounds__(kThreads)
+template <typename V, int UNROLL, int MIN_CTAS>
+__global__ void __launch_bounds__(kThreads, MIN_CTAS)
 reshape_copy_kernel(const char *__restrict__ k, const char *__restrict__ v, long long src_tok,
                     long long src_layer, char *__restrict__ kp, char *__restrict__ vp,
                     long long pool_layer, const long long *__restrict__ slots, long long num_tokens,
@@ -617,7 +617,16 @@ cudaError_t launch_copy_v(const ReshapeLaunch &a, long long entry_bytes, int lay
     const long long pool_layer = a.slots_per_layer * entry_bytes;
     char *kp = static_cast<char *>(a.k_pool) + a.first_layer * pool_layer;
     char *vp = static_cast<char *>(a.v_pool) + a.first_layer * pool_layer;
-    reshape_copy_kernel<V, 4><<<grid, kThreads, 0, st>>>(
+    // Launches that move several layers per item and span more than one
+    // wave run at 2 CTAs per SM with up to 128 registers a thread (100 used):
+    // the all-layer scatter of a 65,536-token chunk reaches 1.007 of the copy
+    // peak against 0.973 at 4 CTAs per SM. A per-layer call (the trait's
+    // write_kv_batch) has one layer per item and keeps 4: measured end to end
+    // from pinned host rows, where each layer's scatter overlaps the next
+    // layer's upload, the 2-CTA form lost 1.3 % of the host link.
+    const bool wide = (long long)grid.x * grid.y > (long long)sms * 4 && layers_per_chunk >= 4;
+    auto kern = wide ? reshape_copy_kernel<V, 4, 2> : reshape_copy_kernel<V, 4, 4>;
+    kern<<<grid, kThreads, 0, st>>>(
         static_cast<const char *>(a.k), static_cast<const char *>(a.v), a.src_token_stride * es,
         a.src_layer_stride * es, kp, vp, pool_layer, a.slots, a.num_tokens, a.slots_per_layer,
         nvec, entry_bytes, (int)a.num_layers, layers_per_chunk, a.err);
