@@ -201,9 +201,9 @@ reshape_fp8_kernel(const char *__restrict__ k, const char *__restrict__ v, long 
 // new_lens, each (token, group) item resolves its slot on chip and quantises
 // its group for every layer of its chunk.
 
-template <typename S, int PER, int UNROLL, int MIN_CTAS>
-__global__ void __launch_bounds__(kThreads, MIN_CTAS)
-resolve_cache_fp8_kernel(ResolveCacheLaunch a, long long groups, int layers_per_chunk) {
+template <typename S, int PER, int UNROLL>
+__device__ __forceinline__ void resolve_cache_fp8_general(const ResolveCacheLaunch &a,
+                                                          long long groups, int layers_per_chunk) {
     extern __shared__ int s_cu[];
     __shared__ int s_warp[kThreads / 32];
     __shared__ int s_bad;
@@ -243,6 +243,98 @@ resolve_cache_fp8_kernel(ResolveCacheLaunch a, long long groups, int layers_per_
             vbase + t * src_tok + l0 * src_layer + e0 * (long long)sizeof(S), src_layer,
             kp + l0 * pool_layer + s * entry + e0, vp + l0 * pool_layer + s * entry + e0, pool_layer,
             l0, l1, a.first_layer, e0, a.fp8);
+    }
+}
+
+template <typename S, int PER, int UNROLL, int MIN_CTAS>
+__global__ void __launch_bounds__(kThreads, MIN_CTAS)
+resolve_cache_fp8_kernel(ResolveCacheLaunch a, long long groups, int layers_per_chunk) {
+    resolve_cache_fp8_general<S, PER, UNROLL>(a, groups, layers_per_chunk);
+}
+
+// The general form compiled on its own: the decode kernel's rarely taken
+// fallback, so that its registers do not weigh on the decode path.
+template <typename S, int UNROLL>
+__device__ __noinline__ void resolve_cache_fp8_general_call(ResolveCacheLaunch a, long long groups,
+                                                            int layers_per_chunk) {
+    resolve_cache_fp8_general<S, 16, UNROLL>(a, groups, layers_per_chunk);
+}
+
+// Decode form (num_tokens == num_seqs, one 16-element group per thread), as
+// resolve_cache_decode_kernel (pkv_kernels.cu): the context length and the
+// first UNROLL layers' source groups are loaded before one barrier vote
+// checks that every new_lens is 1 and every context non-negative; the
+// general form runs otherwise.
+template <typename S, int UNROLL>
+__global__ void __launch_bounds__(kThreads, 4)
+resolve_cache_fp8_decode_kernel(ResolveCacheLaunch a, long long groups, int layers_per_chunk) {
+    const long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool active = it < a.num_tokens * groups;
+    const int l0 = blockIdx.y * layers_per_chunk;
+    const int l1 = min((int)a.num_layers, l0 + layers_per_chunk);
+    const int have = min(UNROLL, l1 - l0);
+    const long long src_tok = a.src_token_stride_bytes, src_layer = a.src_layer_stride_bytes;
+    long long t = 0, e0 = 0;
+    int pos = 0;
+    Group16<S> kg[UNROLL], vg[UNROLL];
+    if (active) {
+        t = it / groups;
+        e0 = (it - t * groups) * 16;
+        pos = __ldg(a.ctx_lens + t);
+        const long long off = t * src_tok + l0 * src_layer + e0 * (long long)sizeof(S);
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u)
+            if (u < have) {
+                kg[u].load(static_cast<const char *>(a.k) + off + u * src_layer);
+                vg[u].load(static_cast<const char *>(a.v) + off + u * src_layer);
+            }
+    }
+    int ok = 1;
+    for (int q = threadIdx.x; q < a.num_seqs; q += kThreads)
+        ok &= (__ldg(a.new_lens + q) == 1) & (__ldg(a.ctx_lens + q) >= 0);
+    if (!__syncthreads_and(ok)) {
+        resolve_cache_fp8_general_call<S, UNROLL>(a, groups, layers_per_chunk);
+        return;
+    }
+    if (blockIdx.x == 0 && blockIdx.y == 0)
+        for (int q = threadIdx.x; q <= a.num_seqs; q += kThreads) a.cu_seqlens[q] = q;
+    if (!active) return;
+    // BlockTable::slot_for_position (block_table.rs:97-101) of position pos.
+    const bool lead = e0 == 0 && blockIdx.y == 0;
+    const long long lb = pos / a.block_size;
+    long long s = -1;
+    if (lb >= a.table_stride) {
+        if (lead) record_error(a.err, kSlotOutOfRange, t);
+    } else {
+        const long long blk = __ldg(a.tables + t * a.table_stride + lb);
+        if (blk < 0 || blk >= a.num_blocks) {
+            if (lead) record_error(a.err, kInvalidBlock, t);
+        } else {
+            s = blk * a.block_size + (pos - lb * a.block_size);
+        }
+    }
+    if (lead && a.slots_out) a.slots_out[t] = s;
+    if (s < 0) return;
+    const long long entry = a.entry_elems;  // one byte per element
+    const long long pool_layer = a.slots_per_layer * entry;
+    const Fp8Scales &sc = a.fp8;
+    const long long head = (sc.elem_offset + e0) / sc.head_dim;
+    const float *ki = sc.k_inv + (a.first_layer + l0) * sc.heads + head;
+    const float *vi = sc.v_inv + (a.first_layer + l0) * sc.heads + head;
+    uint8_t *kd = static_cast<uint8_t *>(a.k_pool) + (a.first_layer + l0) * pool_layer + s * entry + e0;
+    uint8_t *vd = static_cast<uint8_t *>(a.v_pool) + (a.first_layer + l0) * pool_layer + s * entry + e0;
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+        if (u < have) {
+            __stcs(reinterpret_cast<uint4 *>(kd + u * pool_layer), kg[u].quantise(__ldg(ki + u * sc.heads)));
+            __stcs(reinterpret_cast<uint4 *>(vd + u * pool_layer), vg[u].quantise(__ldg(vi + u * sc.heads)));
+        }
+    if (l0 + have < l1) {
+        const long long off = t * src_tok + (l0 + have) * src_layer + e0 * (long long)sizeof(S);
+        quantise_layers<S, 16, UNROLL>(static_cast<const char *>(a.k) + off,
+                                       static_cast<const char *>(a.v) + off, src_layer,
+                                       kd + have * pool_layer, vd + have * pool_layer, pool_layer,
+                                       l0 + have, l1, a.first_layer, e0, sc);
     }
 }
 
@@ -373,9 +465,12 @@ cudaError_t resolve_cache_fp8_s(const ResolveCacheLaunch &a, int sms, cudaStream
     // As resolve_cache_kernel: one wave keeps 4 CTAs per SM, larger launches
     // run at 3 with more registers a thread.
     const bool one_wave = (long long)grid.x * grid.y <= (long long)sms * 4;
-    auto kern = g16 ? (one_wave ? resolve_cache_fp8_kernel<S, 16, unroll_for<S>(), 4>
-                                : resolve_cache_fp8_kernel<S, 16, unroll_for<S>(), 3>)
-                    : resolve_cache_fp8_kernel<S, 1, 1, 4>;
+    // One new token per sequence, every item in the first pass: the decode form.
+    const bool decode = g16 && a.num_tokens == a.num_seqs && (long long)bx * kThreads >= items;
+    auto kern = decode ? resolve_cache_fp8_decode_kernel<S, unroll_for<S>()>
+                : g16 ? (one_wave ? resolve_cache_fp8_kernel<S, 16, unroll_for<S>(), 4>
+                                  : resolve_cache_fp8_kernel<S, 16, unroll_for<S>(), 3>)
+                      : resolve_cache_fp8_kernel<S, 1, 1, 4>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;

@@ -163,17 +163,27 @@ def test_device_scatter_quantises_as_the_oracle(cuda, src, all_layers):
     assert (kdg, vdg) == gpu.digest() == cpu.digest()
 
 
-@pytest.mark.parametrize("head_dim", [128, 8])
-def test_fused_resolve_and_quantise_matches_oracle(cuda, head_dim):
+@pytest.mark.parametrize("head_dim,shape", [(128, "ragged"), (8, "ragged"), (128, "decode"),
+                                            (128, "decode_mixed"), (8, "decode")])
+def test_fused_resolve_and_quantise_matches_oracle(cuda, head_dim, shape):
+    """Ragged batches, and one-token-per-sequence batches: the decode form
+    (every new_lens 1) and its fallback to the general form (lengths that
+    also sum to the sequence count), over 5 layers so that the layers past
+    the prefetched ones are quantised too."""
     import torch
 
-    cfg = CacheConfig(2048, 16, 4, head_dim, 4, 1)
+    cfg = CacheConfig(2048, 16, 4, head_dim, 5, 1)
     cpu, gpu, ks, vs = pair(cfg, seed=11)
     st = Stream(12)
     s = 40
     ctx = st.integers(s, 0, 200).astype(np.int32)
-    new = st.integers(s, 1, 180).astype(np.int32)
-    new[::7] = 0
+    if shape == "ragged":
+        new = st.integers(s, 1, 180).astype(np.int32)
+        new[::7] = 0
+    else:
+        new = np.ones(s, np.int32)
+        if shape == "decode_mixed":
+            new[0], new[1] = 2, 0
     need = -(-(ctx + new) // 16)
     stride = int(need.max())
     perm = st.permutation(cfg.num_blocks)
