@@ -80,3 +80,40 @@ def test_config_errors_are_reported_before_device_work():
         B200Backend(CacheConfig.tiny(8), dtype="bf16")  # tiny says 4 bytes per element
     with pytest.raises(Device, match="shard"):
         B200Backend(CacheConfig.tiny(8), shard_rank=0, num_shards=3)  # 8 elements / 3
+
+
+def test_headers_compile_as_c_and_cpp_and_link(tmp_path):
+    """The C ABI is consumed from C, Rust (bindgen-style declarations) and
+    C++: both headers must compile as strict C99 and C++17, and a C program
+    calling the entry points must link against the library."""
+    import shutil
+    import subprocess
+
+    from pagedkv._lib import LIB_PATH
+
+    inc = ROOT / "include"
+    src = tmp_path / "use.c"
+    src.write_text(
+        "#include <pkv_b200.h>\n#include <pkv_host.h>\n#include <stdio.h>\n"
+        "int main(void) {\n"
+        "  pkv_config c = {16, 16, 2, 64, 2, 2};\n"
+        "  pkv_backend *b = 0;\n"
+        "  int rc = pkv_create(&c, 1, 0, 0, 1, &b);\n"
+        "  printf(\"%d %s\\n\", rc, pkv_last_error());\n"
+        "  if (b) pkv_destroy(b);\n"
+        "  return 0;\n}\n")
+    cc = shutil.which("gcc")
+    cxx = shutil.which("g++")
+    assert cc and cxx
+    for compiler, std in ((cc, "-std=c99"), (cxx, "-std=c++17")):
+        lang = ["-x", "c"] if compiler == cc else ["-x", "c++"]
+        subprocess.run([compiler, *lang, std, "-Wall", "-Wextra", "-Werror", "-pedantic",
+                        "-fsyntax-only", f"-I{inc}", str(src)], check=True)
+    exe = tmp_path / "use"
+    subprocess.run([cc, "-std=c99", f"-I{inc}", str(src), str(LIB_PATH), "-o", str(exe),
+                    f"-Wl,-rpath,{LIB_PATH.parent}"], check=True)
+    assert exe.exists()
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0
+    rc = int(out.stdout.split()[0])  # 0 with a GPU; a device error status without one
+    assert rc == 0 or rc == 9
