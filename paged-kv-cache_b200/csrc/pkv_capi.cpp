@@ -1,11 +1,15 @@
 // pkv_capi.cpp -- the extern "C" surface declared in include/pkv_b200.h.
 // Each entry point records its status (code, the CacheError variant's fields
 // and a message) in thread-local storage and returns the code; no exception
-// crosses the boundary.
+// crosses the boundary. Each call that reaches the backend is an NVTX range
+// named after the entry point (visible to Nsight Systems; free without a
+// tool attached).
 
 #include <cstring>
 #include <exception>
 #include <new>
+
+#include <nvtx3/nvToolsExt.h>
 
 #include "pkv_b200.h"
 #include "pkv_backend.hpp"
@@ -36,8 +40,14 @@ int bad_dtype() { return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "unknown dtype 
 
 cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
 
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+};
+
 template <typename F>
-int guarded(F &&f) {
+int guarded(const char *name, F &&f) {
+    NvtxRange range(name);
     try {
         return finish(f());
     } catch (const std::bad_alloc &) {
@@ -64,7 +74,7 @@ int pkv_create(const pkv_config *cfg, int dtype, int device, int shard_rank, int
     if (!cfg || !out) return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "null argument"));
     *out = nullptr;
     if (!valid_dtype(dtype)) return bad_dtype();
-    return guarded([&] {
+    return guarded("pkv_create", [&] {
         std::unique_ptr<pkv::B200Backend> impl;
         pkv::Status s = pkv::B200Backend::create(*cfg, static_cast<pkv::DType>(dtype), device,
                                                  shard_rank, num_shards, &impl);
@@ -116,7 +126,7 @@ int pkv_write_kv(pkv_backend *b, uint64_t layer, pkv_slot dst, const void *k, ui
                  const void *v, uint64_t v_len, int host_dtype) {
     if (!b) return null_handle();
     if (!valid_dtype(host_dtype)) return bad_dtype();
-    return guarded([&] {
+    return guarded("pkv_write_kv", [&] {
         return b->impl->write_kv(layer, dst, k, k_len, v, v_len, static_cast<pkv::DType>(host_dtype));
     });
 }
@@ -126,7 +136,7 @@ int pkv_write_kv_batch(pkv_backend *b, uint64_t layer, const pkv_slot *dsts, uin
                        int host_dtype) {
     if (!b) return null_handle();
     if (!valid_dtype(host_dtype)) return bad_dtype();
-    return guarded([&] {
+    return guarded("pkv_write_kv_batch", [&] {
         return b->impl->write_kv_batch(layer, dsts, count, k, k_len, v, v_len,
                                        static_cast<pkv::DType>(host_dtype));
     });
@@ -136,7 +146,7 @@ int pkv_read_kv(pkv_backend *b, uint64_t layer, pkv_slot src, void *k_out, uint6
                 void *v_out, uint64_t v_len, int host_dtype) {
     if (!b) return null_handle();
     if (!valid_dtype(host_dtype)) return bad_dtype();
-    return guarded([&] {
+    return guarded("pkv_read_kv", [&] {
         return b->impl->read_kv(layer, src, k_out, k_len, v_out, v_len,
                                 static_cast<pkv::DType>(host_dtype));
     });
@@ -144,22 +154,22 @@ int pkv_read_kv(pkv_backend *b, uint64_t layer, pkv_slot src, void *k_out, uint6
 
 int pkv_copy_block(pkv_backend *b, uint64_t src, uint64_t dst) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->copy_block(src, dst); });
+    return guarded("pkv_copy_block", [&] { return b->impl->copy_block(src, dst); });
 }
 
 int pkv_copy_blocks(pkv_backend *b, const uint64_t *pairs, uint64_t count) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->copy_blocks(pairs, count); });
+    return guarded("pkv_copy_blocks", [&] { return b->impl->copy_blocks(pairs, count); });
 }
 
 int pkv_zero_block(pkv_backend *b, uint64_t block) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->zero_block(block); });
+    return guarded("pkv_zero_block", [&] { return b->impl->zero_block(block); });
 }
 
 int pkv_zero_blocks(pkv_backend *b, const uint64_t *blocks, uint64_t count) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->zero_blocks(blocks, count); });
+    return guarded("pkv_zero_blocks", [&] { return b->impl->zero_blocks(blocks, count); });
 }
 
 int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, const void *v,
@@ -168,7 +178,7 @@ int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, cons
                               void *stream) {
     if (!b) return null_handle();
     if (!valid_dtype(src_dtype)) return bad_dtype();
-    return guarded([&] {
+    return guarded("pkv_reshape_and_cache_dev", [&] {
         return b->impl->reshape_and_cache_dev(layer, k, v, src_token_stride, src_layer_stride,
                                               slot_mapping, num_tokens,
                                               static_cast<pkv::DType>(src_dtype), as_stream(stream));
@@ -177,13 +187,13 @@ int pkv_reshape_and_cache_dev(pkv_backend *b, int64_t layer, const void *k, cons
 
 int pkv_copy_blocks_dev(pkv_backend *b, const int64_t *pairs, int64_t count, void *stream) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->copy_blocks_dev(pairs, count, as_stream(stream)); });
+    return guarded("pkv_copy_blocks_dev", [&] { return b->impl->copy_blocks_dev(pairs, count, as_stream(stream)); });
 }
 
 int pkv_set_kv_scales(pkv_backend *b, const float *k_scales, const float *v_scales,
                       uint64_t count) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->set_kv_scales(k_scales, v_scales, count); });
+    return guarded("pkv_set_kv_scales", [&] { return b->impl->set_kv_scales(k_scales, v_scales, count); });
 }
 
 int pkv_paged_attention_dev(pkv_backend *b, int64_t layer, const void *q, int64_t q_seq_stride,
@@ -192,7 +202,7 @@ int pkv_paged_attention_dev(pkv_backend *b, int64_t layer, const void *q, int64_
                             int64_t max_context_len, float softmax_scale, void *out, float *lse,
                             void *stream) {
     if (!b) return null_handle();
-    return guarded([&] {
+    return guarded("pkv_paged_attention_dev", [&] {
         return b->impl->paged_attention_dev(layer, q, b->impl->dtype(), q_seq_stride, num_seqs,
                                             num_q_heads, block_tables, table_stride, context_lens,
                                             max_context_len, softmax_scale, out, lse,
@@ -207,7 +217,7 @@ int pkv_paged_attention_typed_dev(pkv_backend *b, int64_t layer, const void *q, 
                                   float softmax_scale, void *out, float *lse, void *stream) {
     if (!b) return null_handle();
     if (!valid_dtype(query_dtype)) return bad_dtype();
-    return guarded([&] {
+    return guarded("pkv_paged_attention_typed_dev", [&] {
         return b->impl->paged_attention_dev(layer, q, static_cast<pkv::DType>(query_dtype),
                                             q_seq_stride, num_seqs, num_q_heads, block_tables,
                                             table_stride, context_lens, max_context_len,
@@ -217,12 +227,12 @@ int pkv_paged_attention_typed_dev(pkv_backend *b, int64_t layer, const void *q, 
 
 int pkv_set_copy_engine(pkv_backend *b, int engine) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->set_copy_engine(engine); });
+    return guarded("pkv_set_copy_engine", [&] { return b->impl->set_copy_engine(engine); });
 }
 
 int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, void *stream) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->zero_blocks_dev(blocks, count, as_stream(stream)); });
+    return guarded("pkv_zero_blocks_dev", [&] { return b->impl->zero_blocks_dev(blocks, count, as_stream(stream)); });
 }
 
 int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t table_stride,
@@ -230,7 +240,7 @@ int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t t
                           int64_t num_tokens, int32_t *cu_seqlens, int64_t *slot_mapping,
                           void *stream) {
     if (!b) return null_handle();
-    return guarded([&] {
+    return guarded("pkv_resolve_slots_dev", [&] {
         return b->impl->resolve_slots_dev(block_tables, table_stride, ctx_lens, new_lens, num_seqs,
                                           num_tokens, cu_seqlens, slot_mapping, as_stream(stream));
     });
@@ -244,7 +254,7 @@ int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64
                               void *stream) {
     if (!b) return null_handle();
     if (!valid_dtype(src_dtype)) return bad_dtype();
-    return guarded([&] {
+    return guarded("pkv_resolve_and_cache_dev", [&] {
         return b->impl->resolve_and_cache_dev(block_tables, table_stride, ctx_lens, new_lens,
                                               num_seqs, num_tokens, cu_seqlens, slot_mapping,
                                               layer, k, v, src_token_stride, src_layer_stride,
@@ -255,7 +265,7 @@ int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64
 
 int pkv_digest(pkv_backend *b, uint64_t *k_digest, uint64_t *v_digest, void *stream) {
     if (!b || !k_digest || !v_digest) return null_handle();
-    return guarded([&] { return b->impl->digest(k_digest, v_digest, as_stream(stream)); });
+    return guarded("pkv_digest", [&] { return b->impl->digest(k_digest, v_digest, as_stream(stream)); });
 }
 
 int pkv_digest_rows_dev(pkv_backend *b, int64_t layer, const void *k, const void *v,
@@ -264,7 +274,7 @@ int pkv_digest_rows_dev(pkv_backend *b, int64_t layer, const void *k, const void
                         uint64_t *k_digest, uint64_t *v_digest, void *stream) {
     if (!b || !k_digest || !v_digest) return null_handle();
     if (!valid_dtype(src_dtype)) return bad_dtype();
-    return guarded([&] {
+    return guarded("pkv_digest_rows_dev", [&] {
         return b->impl->digest_rows(layer, k, v, src_token_stride, src_layer_stride, slot_mapping,
                                     num_tokens, static_cast<pkv::DType>(src_dtype), k_digest,
                                     v_digest, as_stream(stream));
@@ -273,12 +283,12 @@ int pkv_digest_rows_dev(pkv_backend *b, int64_t layer, const void *k, const void
 
 int pkv_sync(pkv_backend *b) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->sync(); });
+    return guarded("pkv_sync", [&] { return b->impl->sync(); });
 }
 
 int pkv_device_error(pkv_backend *b, int64_t *index) {
     if (!b) return null_handle();
-    return guarded([&] { return b->impl->take_device_error(index); });
+    return guarded("pkv_device_error", [&] { return b->impl->take_device_error(index); });
 }
 
 }  // extern "C"
