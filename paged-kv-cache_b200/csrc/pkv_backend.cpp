@@ -168,8 +168,14 @@ Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int s
     // issue on the legacy default stream.
     if ((e = cudaStreamCreateWithFlags(&b->stream_, cudaStreamDefault)) != cudaSuccess)
         return device_error("cudaStreamCreate", e);
+    // Uploads of the caller's host rows into private staging need no order
+    // with other streams' work: a non-blocking stream.
+    if ((e = cudaStreamCreateWithFlags(&b->copy_stream_, cudaStreamNonBlocking)) != cudaSuccess)
+        return device_error("cudaStreamCreate", e);
     if ((e = cudaEventCreateWithFlags(&b->h_stage_free_, cudaEventDisableTiming)) != cudaSuccess ||
-        (e = cudaEventCreateWithFlags(&b->inputs_consumed_, cudaEventDisableTiming)) != cudaSuccess)
+        (e = cudaEventCreateWithFlags(&b->inputs_consumed_, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&b->scatter_free_[0], cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&b->scatter_free_[1], cudaEventDisableTiming)) != cudaSuccess)
         return device_error("cudaEventCreate", e);
 
     const size_t plane = static_cast<size_t>(plane_bytes);
@@ -208,6 +214,7 @@ Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int s
 B200Backend::~B200Backend() {
     DeviceGuard g(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    if (copy_stream_) cudaStreamSynchronize(copy_stream_);
     if (k_plane_) cudaFree(k_plane_);
     if (v_plane_) cudaFree(v_plane_);
     if (d_err_) cudaFree(d_err_);
@@ -217,6 +224,11 @@ B200Backend::~B200Backend() {
     if (h_stage_) cudaFreeHost(h_stage_);
     if (h_stage_free_) cudaEventDestroy(h_stage_free_);
     if (inputs_consumed_) cudaEventDestroy(inputs_consumed_);
+    for (int i = 0; i < 2; ++i) {
+        if (d_scatter_[i]) cudaFree(d_scatter_[i]);
+        if (scatter_free_[i]) cudaEventDestroy(scatter_free_[i]);
+    }
+    if (copy_stream_) cudaStreamDestroy(copy_stream_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -231,7 +243,7 @@ uint64_t B200Backend::allocated_bytes() const {
 }
 
 std::string B200Backend::device_name() const {
-    static const char *names[] = {"f32", "bf16", "f16"};
+    static const char *names[] = {"f32", "bf16", "f16", "fp8_e4m3"};
     std::string s = "cuda:" + std::to_string(device_) + " (" + gpu_name_ + ", " +
                     names[static_cast<int>(dtype_)];
     if (num_shards_ > 1)
@@ -264,13 +276,30 @@ Status B200Backend::ensure_device_stage(size_t bytes) {
     if (bytes <= d_stage_bytes_) return Status::Ok();
     cudaError_t e = cudaStreamSynchronize(stream_);  // old buffer may still be read
     if (e != cudaSuccess) return device_error("cudaStreamSynchronize", e);
+    const size_t want = std::max(bytes, d_stage_bytes_ + d_stage_bytes_ / 2);
     if (d_stage_) cudaFree(d_stage_);
     d_stage_ = nullptr;
     d_stage_bytes_ = 0;
-    const size_t want = std::max(bytes, d_stage_bytes_ + d_stage_bytes_ / 2);
     if ((e = cudaMalloc(&d_stage_, want)) != cudaSuccess)
         return device_error("allocating " + std::to_string(want) + " bytes of staging", e);
     d_stage_bytes_ = want;
+    return Status::Ok();
+}
+
+Status B200Backend::ensure_scatter_stage(int buf, size_t bytes) {
+    if (bytes <= d_scatter_bytes_[buf]) return Status::Ok();
+    // The old buffer may still be written by an upload or read by a scatter.
+    cudaError_t e;
+    if ((e = cudaStreamSynchronize(copy_stream_)) != cudaSuccess ||
+        (e = cudaStreamSynchronize(stream_)) != cudaSuccess)
+        return device_error("cudaStreamSynchronize", e);
+    const size_t want = std::max(bytes, d_scatter_bytes_[buf] + d_scatter_bytes_[buf] / 2);
+    if (d_scatter_[buf]) cudaFree(d_scatter_[buf]);
+    d_scatter_[buf] = nullptr;
+    d_scatter_bytes_[buf] = 0;
+    if ((e = cudaMalloc(&d_scatter_[buf], want)) != cudaSuccess)
+        return device_error("allocating " + std::to_string(want) + " bytes of staging", e);
+    d_scatter_bytes_[buf] = want;
     return Status::Ok();
 }
 
@@ -298,7 +327,8 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
     const size_t row_bytes = shard_entry_ * dtype_size(host);
     const size_t slot_bytes = round_up(count * sizeof(int64_t), kAlign);
     const size_t kv_bytes = round_up(count * row_bytes, kAlign);
-    Status s = ensure_device_stage(slot_bytes + 2 * kv_bytes);
+    const int buf = scatter_turn_;
+    Status s = ensure_scatter_stage(buf, slot_bytes + 2 * kv_bytes);
     if (s.ok()) s = ensure_host_stage(count * sizeof(int64_t));
     if (!s.ok()) {
         // A batch whose first destination is invalid writes nothing and needs
@@ -306,19 +336,23 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
         Status first = validate(layer, dsts[0]);
         return first.ok() ? s : first;
     }
-    char *d = static_cast<char *>(d_stage_);
+    scatter_turn_ ^= 1;
+    char *d = static_cast<char *>(d_scatter_[buf]);
     int64_t *d_slots = reinterpret_cast<int64_t *>(d);
     char *d_k = d + slot_bytes;
     char *d_v = d_k + kv_bytes;
 
-    // The K/V rows go to the device first, so that the copy engine moves them
-    // while the host validates the destinations and builds the slot list.
-    // Rows past a failing destination are copied too but never scattered.
+    // The K/V rows go to the device first, on the upload stream, so that the
+    // copy engine moves them while the host validates the destinations and
+    // builds the slot list, and while the previous call's scatter (which read
+    // the other staging buffer) still runs. Rows past a failing destination
+    // are copied too but never scattered.
     cudaError_t e;
-    if ((e = cudaMemcpyAsync(d_k, k, count * row_bytes, cudaMemcpyHostToDevice, stream_)) ||
-        (e = cudaMemcpyAsync(d_v, v, count * row_bytes, cudaMemcpyHostToDevice, stream_)) ||
-        (e = cudaEventRecord(inputs_consumed_, stream_))) {
-        cudaStreamSynchronize(stream_);  // never return while a copy may still read the caller's rows
+    if ((e = cudaStreamWaitEvent(copy_stream_, scatter_free_[buf], 0)) ||
+        (e = cudaMemcpyAsync(d_k, k, count * row_bytes, cudaMemcpyHostToDevice, copy_stream_)) ||
+        (e = cudaMemcpyAsync(d_v, v, count * row_bytes, cudaMemcpyHostToDevice, copy_stream_)) ||
+        (e = cudaEventRecord(inputs_consumed_, copy_stream_))) {
+        cudaStreamSynchronize(copy_stream_);  // never return while a copy may still read the caller's rows
         return device_error("staging K/V", e);
     }
     // The caller's slices are borrowed: return only once they have been read.
@@ -356,7 +390,8 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
             if (hs[i] >= 0) seen_[(uint64_t)hs[i] >> 6] = 0;
     }
     if ((e = cudaMemcpyAsync(d_slots, hs, valid * sizeof(int64_t), cudaMemcpyHostToDevice, stream_)) ||
-        (e = cudaEventRecord(h_stage_free_, stream_)))
+        (e = cudaEventRecord(h_stage_free_, stream_)) ||
+        (e = cudaStreamWaitEvent(stream_, inputs_consumed_, 0)))
         return finish_with(device_error("staging slots", e));
 
     ReshapeLaunch a{};
@@ -376,7 +411,8 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
     a.pool_dtype = dtype_;
     a.err = d_err_;
     a.fp8 = fp8_scales();
-    if ((e = launch_reshape(a, sms_, stream_)) != cudaSuccess)
+    if ((e = launch_reshape(a, sms_, stream_)) != cudaSuccess ||
+        (e = cudaEventRecord(scatter_free_[buf], stream_)) != cudaSuccess)
         return finish_with(device_error("reshape_and_cache", e));
     return finish_with(bad);
 }

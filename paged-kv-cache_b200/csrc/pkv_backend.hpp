@@ -104,6 +104,7 @@ class B200Backend {
     Status validate_block(uint64_t block) const;
     Status validate(uint64_t layer, pkv_slot at) const;
     Status ensure_device_stage(size_t bytes);
+    Status ensure_scatter_stage(int buf, size_t bytes);
     Status ensure_host_stage(size_t bytes);
     Status launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_t count, const void *k,
                           const void *v, DType host);
@@ -136,6 +137,15 @@ class B200Backend {
     size_t h_stage_bytes_ = 0;
     cudaEvent_t h_stage_free_ = nullptr;  // last H2D out of h_stage_ has finished
     cudaEvent_t inputs_consumed_ = nullptr;
+    // Host-path K/V uploads run on their own stream into two alternating
+    // staging buffers, so that a call's upload overlaps the scatter of the
+    // call before it; scatter_free_[i] marks the end of the last scatter
+    // that read buffer i.
+    cudaStream_t copy_stream_ = nullptr;
+    void *d_scatter_[2] = {nullptr, nullptr};
+    size_t d_scatter_bytes_[2] = {0, 0};
+    cudaEvent_t scatter_free_[2] = {nullptr, nullptr};
+    int scatter_turn_ = 0;
     std::vector<uint64_t> seen_;  // one bit per slot of a layer: duplicate detection
     // fp8 pools: [num_layers][num_kv_heads] scales on the host, and their f32
     // reciprocals on the device (K's, then V's).
