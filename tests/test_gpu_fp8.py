@@ -291,3 +291,10 @@ def test_scale_validation(cuda):
     k, v = gpu.read_entry(1, (2, 3))
     np.testing.assert_array_equal(k, np.full(32, 3.0, np.float32))  # 1.5 * 2
     np.testing.assert_array_equal(v, np.full(32, 3.0, np.float32))  # 6 * 0.5
+
+
+def test_device_name_of_an_fp8_pool(cuda):
+    """KvBackend::device_name (backend.rs:123) names the pool dtype."""
+    b = B200Backend(CacheConfig(8, 16, 2, 64, 1, 1), dtype="fp8_e4m3")
+    name = b.device_name()
+    assert "fp8_e4m3" in name and name.startswith("cuda:")
