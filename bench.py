@@ -68,6 +68,9 @@ def parse():
                         "the same pool, for comparison")
     p.add_argument("--copy-engine", choices=["auto", "vector", "bulk"], default="auto",
                    help="cow/churn: copy_blocks engine (pkv_set_copy_engine)")
+    p.add_argument("--q-len", type=int, default=1,
+                   help="attention: query tokens per sequence (the last q_len positions, causal; "
+                        "q_len * 7 <= 16)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-ops", action="store_true")
@@ -590,7 +593,12 @@ def wl_attention(run) -> dict:
     L, D = cfg.num_layers, cfg.head_dim
     kvh = backend.shard_entry_elems // D
     hq = kvh * 7  # Qwen2-7B: 28 query heads over 4 kv heads
+    ql = args.q_len
+    if ql < 1 or ql * 7 > 16:
+        raise SystemExit("attention workload: q_len * 7 query heads per kv head must be <= 16")
     lens = (ctx + new).astype(np.int32)  # the appended token is in the cache too
+    if int(lens.min()) < ql:  # the query tokens are the last q_len of each context
+        raise SystemExit("attention workload: a context is shorter than q_len")
     S = len(lens)
     max_ctx = int(lens.max())
     gen = torch.Generator(device=dev).manual_seed(3000 + run.rank)
@@ -611,19 +619,20 @@ def wl_attention(run) -> dict:
             for l in range(L):
                 x = torch.randn(p_[l].shape, generator=gen, device=dev)
                 p_[l].copy_((x * 3).to(torch.float8_e4m3fn) if fp8 else x.to(torch.bfloat16))
-        q = torch.randn((S, hq, D), generator=gen, device=dev).to(torch.bfloat16)
+        q = torch.randn((S * ql, hq, D), generator=gen, device=dev).to(torch.bfloat16)
     stream.synchronize()
     d_tab = torch.from_numpy(tables).to(dev)
     d_len = torch.from_numpy(lens).to(dev)
-    out = torch.empty((L, S, hq, D), dtype=torch.bfloat16, device=dev)
-    lse = torch.empty((L, S, hq), dtype=torch.float32, device=dev)
+    out = torch.empty((L, S * ql, hq, D), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((L, S * ql, hq), dtype=torch.float32, device=dev)
 
     def step(i, ev):
         if ev is not None:
             ev.extend(torch.cuda.Event(enable_timing=True) for _ in range(2))
             ev[0].record(stream)
         for l in range(L):
-            backend.paged_attention(q, d_tab, d_len, max_ctx, out[l], l, lse=lse[l], stream=stream)
+            backend.paged_attention(q, d_tab, d_len, max_ctx, out[l], l, lse=lse[l], stream=stream,
+                                    q_len=ql)
         if ev is not None:
             ev[1].record(stream)
 
@@ -647,9 +656,11 @@ def wl_attention(run) -> dict:
                 kk = kk * scales[0][l].view(1, kvh, 1)
                 vv = vv * scales[1][l].view(1, kvh, 1)
             kk, vv = kk.repeat_interleave(7, 1), vv.repeat_interleave(7, 1)
-            sc = torch.einsum("hd,thd->ht", q[s_].float(), kk) * D ** -0.5
-            ref = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), vv)
-            worst = max(worst, float((out[l, s_].float() - ref).abs().max()))
+            for i in range(ql):  # query token i sees keys 0 .. n - ql + i
+                m, r = n - ql + i + 1, s_ * ql + i
+                sc = torch.einsum("hd,thd->ht", q[r].float(), kk[:m]) * D ** -0.5
+                ref = torch.einsum("ht,thd->hd", torch.softmax(sc, -1), vv[:m])
+                worst = max(worst, float((out[l, r].float() - ref).abs().max()))
     if worst > 2e-2:
         raise SystemExit(f"attention spot check failed: max abs error {worst}")
 
@@ -660,7 +671,8 @@ def wl_attention(run) -> dict:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             for l in range(L):
-                backend.paged_attention(q, d_tab, d_len, max_ctx, out[l], l, lse=lse[l], stream=stream)
+                backend.paged_attention(q, d_tab, d_len, max_ctx, out[l], l, lse=lse[l], stream=stream,
+                                        q_len=ql)
         torch.cuda.synchronize()
 
         def step(i, ev):  # noqa: F811
@@ -675,13 +687,14 @@ def wl_attention(run) -> dict:
     total_ms, evs, clocks = run.timed_steps(step, K)
     kernel_ms = run.max_over_ranks(_event_ms(evs, 0, 1))
     kv_bytes = int(lens.sum()) * backend.shard_entry_elems * 2 * backend.elem_bytes  # K and V, per layer
-    io_bytes = S * hq * D * 2 * 2 + S * hq * 4 + tables.nbytes + lens.nbytes
+    io_bytes = S * ql * (hq * D * 2 * 2 + hq * 4) + tables.nbytes + lens.nbytes
     alg = L * (kv_bytes + io_bytes)
     workload = (f"decode attention x{world}: {world}x256 sequences, context U[1,4096]+1 "
                 f"(mean {lens.mean():.0f}), Qwen2-7B (28 query heads over 4 kv heads x 128, "
                 f"{L} layers, bs 16, bf16 queries), pool {cfg.num_blocks} blocks "
                 + ("of E4M3 codes with per-(layer, kv head) scales" if fp8 else "bf16")
                 + f" head-sharded {world} ways; step = paged attention over every layer"
+                + (f" with its last {ql} tokens as causal query tokens" if ql > 1 else "")
                 + (" replayed as one CUDA graph" if graph is not None else ""))
     out_line = base_line(run, int(lens.sum()) * world * K / (total_ms / 1e3), K, total_ms / K,
                          "weak", workload, {
@@ -700,7 +713,8 @@ def wl_attention(run) -> dict:
     out_line["gpu_launches"] = K * L * 2
     out_line["spot_check_max_abs_err"] = worst
     out_line["config"]["pool_dtype"] = "fp8_e4m3" if fp8 else "bf16"
-    if args.compare_library and world == 1 and not fp8:
+    out_line["config"]["q_len"] = ql
+    if args.compare_library and world == 1 and not fp8 and ql == 1:
         out_line["library_comparison"] = flashinfer_decode(backend, q, tables, lens, out, L, stream,
                                                            kernel_ms / L, kv_bytes)
     graph = None  # release the captured graph before the backend's buffers go

@@ -267,6 +267,22 @@ int pkv_paged_attention_typed_dev(pkv_backend *b, int64_t layer, const void *q, 
                                   const int32_t *block_tables, int64_t table_stride,
                                   const int32_t *context_lens, int64_t max_context_len,
                                   float softmax_scale, void *out, float *lse, void *stream);
+/* pkv_paged_attention_typed_dev with q_len query tokens per sequence (the
+ * verification step of speculative decoding, or a short chunk of prefill):
+ * query token i of sequence s sits at position context_lens[s] - q_len + i
+ * (its own K/V already in the cache) and attends keys 0 .. that position.
+ * q and out are [num_seqs * q_len][num_q_heads][head_dim], token i of
+ * sequence s at row s * q_len + i; q_token_stride is q's row pitch in
+ * elements (<= 0: dense); lse is [num_seqs * q_len][num_q_heads]. Needs
+ * 1 <= q_len and q_len * (num_q_heads / kv_heads) <= 16. A context shorter
+ * than q_len is recorded as ShapeMismatch and yields zeros. q_len 1 is
+ * pkv_paged_attention_typed_dev. No counterpart in the reference. */
+int pkv_paged_attention_multi_dev(pkv_backend *b, int64_t layer, const void *q, int query_dtype,
+                                  int64_t q_len, int64_t q_token_stride, int64_t num_seqs,
+                                  int64_t num_q_heads, const int32_t *block_tables,
+                                  int64_t table_stride, const int32_t *context_lens,
+                                  int64_t max_context_len, float softmax_scale, void *out,
+                                  float *lse, void *stream);
 
 /* Order-independent 64-bit digests of this backend's K and V planes (the
  * element's global index in the full plane and its f32-widened bits, summed;

@@ -14,10 +14,24 @@ from __future__ import annotations
 import numpy as np
 
 
-def paged_attention(k_plane, v_plane, layer: int, q, tables, ctx, scale: float, head_dim: int):
+def paged_attention(k_plane, v_plane, layer: int, q, tables, ctx, scale: float, head_dim: int,
+                    q_len: int = 1):
     """k_plane, v_plane: [L][num_blocks][block_size][entry] (this backend's
-    heads); q: [S][Hq][D]. Returns (out [S][Hq][D] f64, lse [S][Hq] f64,
-    natural log, -inf for an empty context)."""
+    heads); q: [S][Hq][D], or [S * q_len][Hq][D] with q_len query tokens per
+    sequence: query i of sequence s sits at position ctx[s] - q_len + i and
+    attends to the keys at positions 0 .. ctx[s] - q_len + i (causal over the
+    sequence's last q_len tokens). Returns (out f64 shaped as q, lse [rows][Hq]
+    f64, natural log, -inf for an empty context)."""
+    if q_len > 1:
+        q = np.asarray(q, dtype=np.float64)
+        out = np.zeros(q.shape)
+        lse = np.full(q.shape[:2], -np.inf)
+        for i in range(q_len):
+            lim = np.maximum(np.asarray(ctx) - q_len + i + 1, 0)
+            o, l = paged_attention(k_plane, v_plane, layer, q[i::q_len], tables, lim, scale,
+                                   head_dim)
+            out[i::q_len], lse[i::q_len] = o, l
+        return out, lse
     k_plane = np.asarray(k_plane)
     bs = k_plane.shape[2]
     kvh = k_plane.shape[3] // head_dim

@@ -36,6 +36,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cfloat>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -244,11 +245,12 @@ __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float x) { re
 template <>
 __device__ __forceinline__ __half from_float<__half>(float x) { return __float2half_rn(x); }
 
-// Sequence length as the kernels use it: out-of-range lengths are recorded
-// once and treated as empty.
+// Sequence length as the kernels use it: out-of-range lengths (and, with
+// several query tokens per sequence, a context shorter than the query
+// tokens) are recorded once and treated as empty.
 __device__ __forceinline__ int checked_ctx(const AttnLaunch &a, int seq, bool report) {
     const int ctx = __ldg(a.ctx + seq);
-    if (ctx < 0 || ctx > a.max_ctx) {
+    if (ctx < 0 || ctx > a.max_ctx || (a.q_len > 1 && ctx < a.q_len)) {
         if (report) record_error(a.err, kShapeMismatch, seq);
         return 0;
     }
@@ -259,7 +261,9 @@ __device__ __forceinline__ int checked_ctx(const AttnLaunch &a, int seq, bool re
 // kv head) scales; the tiles are converted to f16 in registers and the math
 // runs in f16 (queries too, scaled by a power of two into f16 range), with
 // the K scale folded into the softmax scale and the V scale into the output.
-template <typename T, int D, int NT, bool FP8>
+// MQ: several query tokens per sequence (a.q_len > 1), causal among
+// themselves; without it the kernel is the one-token decode form.
+template <typename T, int D, int NT, bool FP8, bool MQ>
 __global__ void __launch_bounds__(kAttnThreads, attn_min_ctas<D, FP8>(NT))
 paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                        const AttnLaunch a) {
@@ -285,8 +289,19 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (split > 0 && b0 >= b1) return;  // beyond this sequence's splits: the combine skips it
 
-    // Query tile: row r < group is query head kvh * group + r; other rows zero.
-    const T *q = static_cast<const T *>(a.q) + (long long)seq * a.q_seq_stride + (long long)kvh * a.group * D;
+    // Query tile: row r < cols is query token r / group (of the sequence's
+    // q_len) and head kvh * group + r % group; other rows zero.
+    const int cols = MQ ? a.q_len * a.group : a.group;
+    const T *q = static_cast<const T *>(a.q) + (long long)seq * (MQ ? a.q_len : 1) * a.q_seq_stride +
+                 (long long)kvh * a.group * D;
+    auto q_row = [&](int r) {
+        if constexpr (MQ) {
+            const int i = r / a.group;
+            return q + (long long)i * a.q_seq_stride + (long long)(r - i * a.group) * D;
+        } else {
+            return q + (long long)r * D;
+        }
+    };
     float c = a.scale_log2;
     float v_scale = 1.f;
     if constexpr (FP8) {
@@ -296,9 +311,9 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         if (threadIdx.x == 0) s_qmax = 0;
         __syncthreads();
         float mx = 0.f;
-        for (int i = threadIdx.x; i < a.group * (D / 8); i += kAttnThreads) {
+        for (int i = threadIdx.x; i < cols * (D / 8); i += kAttnThreads) {
             const int r = i / (D / 8), cc = i - r * (D / 8);
-            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(q + (long long)r * D) + cc);
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(q_row(r)) + cc);
             const T *e = reinterpret_cast<const T *>(&v);
 #pragma unroll
             for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(to_float(e[k])));
@@ -317,8 +332,8 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         for (int i = threadIdx.x; i < 16 * (D / 8); i += kAttnThreads) {
             const int r = i / (D / 8), cc = i - r * (D / 8);
             uint4 v = make_uint4(0, 0, 0, 0);
-            if (r < a.group) {
-                const uint4 x = __ldg(reinterpret_cast<const uint4 *>(q + (long long)r * D) + cc);
+            if (r < cols) {
+                const uint4 x = __ldg(reinterpret_cast<const uint4 *>(q_row(r)) + cc);
                 const T *xe = reinterpret_cast<const T *>(&x);
                 uint32_t *w = reinterpret_cast<uint32_t *>(&v);
 #pragma unroll
@@ -331,7 +346,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         for (int i = threadIdx.x; i < 16 * (D / 8); i += kAttnThreads) {
             const int r = i / (D / 8), cc = i - r * (D / 8);
             uint4 v = make_uint4(0, 0, 0, 0);
-            if (r < a.group) v = __ldg(reinterpret_cast<const uint4 *>(q + (long long)r * D) + cc);
+            if (r < cols) v = __ldg(reinterpret_cast<const uint4 *>(q_row(r)) + cc);
             *reinterpret_cast<uint4 *>(qs + r * G::kQPitch + cc * 16) = v;
         }
     }
@@ -451,9 +466,27 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int mt = 0; mt < D / 16; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
+    // With several query tokens the reference points start at -FLT_MAX
+    // rather than -inf, so that a head whose scores are all masked in a block
+    // (a query token before the block's first key) keeps finite arithmetic:
+    // its weights are 2^-inf = 0. With one token every block holds a key of
+    // every head.
     float mc[NT][2], l_run[NT][2];
+    constexpr float kM0 = MQ ? -FLT_MAX : -INFINITY;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) mc[nt][0] = mc[nt][1] = -INFINITY, l_run[nt][0] = l_run[nt][1] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) mc[nt][0] = mc[nt][1] = kM0, l_run[nt][0] = l_run[nt][1] = 0.f;
+    // Query token index of this lane's two columns per n-tile, 4 bits each
+    // (q_len * group <= 16); padding columns take the last token's limit.
+    uint32_t qcols = 0;
+    if constexpr (MQ) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {
+                const int col = nt * 8 + (lane & 3) * 2 + hc;
+                qcols |= (uint32_t)(col < cols ? col / a.group : a.q_len - 1) << (4 * (2 * nt + hc));
+            }
+    }
     uint32_t phase = 0;  // bit s: parity of stage s's next completion
     bool failed = false;
 
@@ -483,7 +516,8 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         }
         if (ready && !failed) {
             const uint32_t kb = ring_u32 + st * G::kStageBytes;
-            const int valid = min(kTok, ctx - (first + kAttnWarps * n) * kTok);
+            const int kb0 = (first + kAttnWarps * n) * kTok;  // the block's first key
+            const int valid = min(kTok, ctx - kb0);
 
             // S^T[token][head] for the block's 16 tokens, even and odd
             // k-steps in separate accumulators (shorter mma chains).
@@ -523,15 +557,10 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) sc[nt][e] += s2[nt][e];
-            if (valid < kTok) {
-                // The sequence ends inside this block: mask the tokens past
-                // its end, and zero their V rows (they may hold anything, NaN
-                // included) so that their zero weights contribute exactly 0.
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    if (g >= valid) sc[nt][0] = sc[nt][1] = -INFINITY;
-                    if (g + 8 >= valid) sc[nt][2] = sc[nt][3] = -INFINITY;
-                }
+            // Zeroes the V rows past the sequence's end (they may hold
+            // anything, NaN included) so that their zero weights contribute
+            // exactly 0.
+            auto zero_tail = [&]() {
                 unsigned char *vb = ring + st * G::kStageBytes + G::kTileBytes;
                 constexpr int kChunks = G::kBoxRow / 16;  // per row and box
                 for (int i = lane; i < (kTok - valid) * G::kBoxes * kChunks; i += 32) {
@@ -541,6 +570,32 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                 }
                 dirty |= 1u << st;
                 __syncwarp();
+            };
+            if constexpr (MQ) {
+                // Token i attends keys up to ctx - q_len + i; last0 is token
+                // 0's limit relative to the block. Where some token's limit
+                // falls inside the block, mask each column past its own.
+                const int last0 = ctx - a.q_len - kb0;
+                if (last0 < kTok - 1) {
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int hc = 0; hc < 2; ++hc) {
+                            const int lim = last0 + (int)((qcols >> (4 * (2 * nt + hc))) & 15u);
+                            if (g > lim) sc[nt][hc] = -INFINITY;
+                            if (g + 8 > lim) sc[nt][2 + hc] = -INFINITY;
+                        }
+                    if (valid < kTok) zero_tail();
+                }
+            } else if (valid < kTok) {
+                // The sequence ends inside this block: mask the tokens past
+                // its end.
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    if (g >= valid) sc[nt][0] = sc[nt][1] = -INFINITY;
+                    if (g + 8 >= valid) sc[nt][2] = sc[nt][3] = -INFINITY;
+                }
+                zero_tail();
             }
             // Online softmax per query head (a column of S^T, spread over the
             // 8 lanes with the same j) in base 2: p = 2^(s * c - m). The
@@ -567,7 +622,9 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
                         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
                         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
                         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                        const float m_new = fmaxf(mc[nt][hc], mx * c);  // finite: token 0 is valid
+                        // Finite: one token's blocks all hold a key of the
+                        // head; several tokens' mc starts at -FLT_MAX.
+                        const float m_new = fmaxf(mc[nt][hc], mx * c);
                         const float corr = ex2(mc[nt][hc] - m_new);
                         l_run[nt][hc] *= corr;
 #pragma unroll
@@ -668,7 +725,7 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     }
     __syncthreads();
     failed = s_failed != 0;  // a timed-out wait in any warp voids the CTA's result
-    for (int idx = threadIdx.x; idx < a.group * D; idx += kAttnThreads) {
+    for (int idx = threadIdx.x; idx < cols * D; idx += kAttnThreads) {
         const int row = idx / D, d = idx - row * D;
         float M = -INFINITY;
 #pragma unroll
@@ -684,8 +741,9 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         }
         const float val = (L > 0.f && !failed) ? acc / L * v_scale : 0.f;
         const float lse2 = (L > 0.f && !failed) ? M + log2f(L) : -INFINITY;
-        const long long qh = (long long)kvh * a.group + row;
-        const long long sq = (long long)seq * a.num_q_heads + qh;
+        const int qi = MQ ? row / a.group : 0;  // query token of the row
+        const long long qh = (long long)kvh * a.group + (row - qi * a.group);
+        const long long sq = ((long long)seq * (MQ ? a.q_len : 1) + qi) * a.num_q_heads + qh;
         if (a.num_splits == 1) {
             static_cast<T *>(a.out)[sq * D + d] = from_float<T>(val);
             if (d == 0 && a.lse) a.lse[sq] = lse2 * 0.69314718055994531f;
@@ -696,13 +754,13 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     }
 }
 
-// Merges the splits of one sequence, all its query heads: per head the
-// weights 2^(lse_i - max) / sum go to shared memory, then every thread
-// combines float4 runs of the partial outputs.
+// Merges the splits of one sequence, all its query tokens and heads: per
+// (token, head) row the weights 2^(lse_i - max) / sum go to shared memory,
+// then every thread combines float4 runs of the partial outputs.
 template <typename T, int D>
 __global__ void __launch_bounds__(256)
 paged_attention_combine_kernel(const AttnLaunch a) {
-    extern __shared__ float s_w[];  // [num_q_heads][num_splits]
+    extern __shared__ float s_w[];  // [q_len * num_q_heads][num_splits]
     // Launched as a programmatic dependent of the attention grid: its CTAs
     // can take SM slots while the attention's last CTAs run, and wait here
     // until that grid has completed and its partials are visible.
@@ -711,8 +769,9 @@ paged_attention_combine_kernel(const AttnLaunch a) {
     const int ctx = checked_ctx(a, seq, false);
     const int nblk = (ctx + kTok - 1) / kTok;
     const int used = max(1, (nblk + a.blocks_per_split - 1) / a.blocks_per_split);
-    for (int h = threadIdx.x; h < a.num_q_heads; h += blockDim.x) {
-        const long long sq = (long long)seq * a.num_q_heads + h;
+    const int rows = a.q_len * a.num_q_heads;  // the sequence's output rows, contiguous
+    for (int h = threadIdx.x; h < rows; h += blockDim.x) {
+        const long long sq = (long long)seq * rows + h;
         const float *lse = a.part_lse + sq * a.num_splits;
         float M = -INFINITY;
         for (int i = 0; i < used; ++i) M = fmaxf(M, lse[i]);
@@ -724,9 +783,9 @@ paged_attention_combine_kernel(const AttnLaunch a) {
         if (a.lse) a.lse[sq] = den > 0.f ? (M + log2f(den)) * 0.69314718055994531f : -INFINITY;
     }
     __syncthreads();
-    for (int it = threadIdx.x; it < a.num_q_heads * (D / 4); it += blockDim.x) {
+    for (int it = threadIdx.x; it < rows * (D / 4); it += blockDim.x) {
         const int h = it / (D / 4), d4 = it - h * (D / 4);
-        const long long sq = (long long)seq * a.num_q_heads + h;
+        const long long sq = (long long)seq * rows + h;
         const float4 *po = reinterpret_cast<const float4 *>(a.part_o + sq * a.num_splits * D) + d4;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int i = 0; i < used; ++i) {
@@ -744,10 +803,10 @@ paged_attention_combine_kernel(const AttnLaunch a) {
     }
 }
 
-template <typename T, int D, int NT, bool FP8>
+template <typename T, int D, int NT, bool FP8, bool MQ>
 cudaError_t launch_main(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t st) {
     using G = AttnGeom<D, FP8, attn_stages<D, FP8>(NT)>;
-    auto kern = paged_attention_kernel<T, D, NT, FP8>;
+    auto kern = paged_attention_kernel<T, D, NT, FP8, MQ>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)a.num_splits, (unsigned)a.kv_heads, (unsigned)a.num_seqs);
@@ -757,11 +816,15 @@ cudaError_t launch_main(const AttnLaunch &a, const CUtensorMap *maps, cudaStream
 
 template <typename T, int D, bool FP8>
 cudaError_t launch_td(const AttnLaunch &a, const CUtensorMap *maps, cudaStream_t st) {
-    cudaError_t e = a.group <= 8 ? launch_main<T, D, 1, FP8>(a, maps, st)
-                                 : launch_main<T, D, 2, FP8>(a, maps, st);
+    if (a.q_len < 1 || a.q_len * a.group > 16) return cudaErrorInvalidValue;
+    const bool nt1 = a.q_len * a.group <= 8;
+    cudaError_t e = a.q_len == 1 ? (nt1 ? launch_main<T, D, 1, FP8, false>(a, maps, st)
+                                        : launch_main<T, D, 2, FP8, false>(a, maps, st))
+                                 : (nt1 ? launch_main<T, D, 1, FP8, true>(a, maps, st)
+                                        : launch_main<T, D, 2, FP8, true>(a, maps, st));
     if (e != cudaSuccess) return e;
     if (a.num_splits > 1) {
-        const size_t smem = (size_t)a.num_q_heads * a.num_splits * sizeof(float);
+        const size_t smem = (size_t)a.q_len * a.num_q_heads * a.num_splits * sizeof(float);
         if (smem > 227 * 1024) return cudaErrorInvalidValue;
         if (smem > 48 * 1024 &&
             (e = cudaFuncSetAttribute(paged_attention_combine_kernel<T, D>,

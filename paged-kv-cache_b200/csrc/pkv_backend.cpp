@@ -897,7 +897,7 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType quer
                                         int64_t num_seqs, int64_t num_q_heads,
                                         const int32_t *tables, int64_t table_stride,
                                         const int32_t *ctx, int64_t max_ctx, float softmax_scale,
-                                        void *out, float *lse, cudaStream_t st) {
+                                        void *out, float *lse, cudaStream_t st, int64_t q_len) {
     if (layer < 0 || (uint64_t)layer >= cfg_.num_layers)
         return error(PKV_ERR_INVALID_LAYER, layer, (int64_t)cfg_.num_layers,
                      msg_layer((uint64_t)layer, cfg_.num_layers));
@@ -923,6 +923,9 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType quer
     const int64_t group = num_q_heads / kv;
     if (group > 16)
         return error(PKV_ERR_DEVICE, 0, 0, "paged attention supports at most 16 query heads per kv head");
+    if (q_len < 1 || q_len * group > 16)
+        return error(PKV_ERR_DEVICE, 0, 0,
+                     "paged attention takes 1 <= q_len and q_len * (query heads per kv head) <= 16");
     if (num_seqs == 0) return Status::Ok();
     if (num_seqs > 65535) return error(PKV_ERR_DEVICE, 0, 0, "at most 65535 sequences per call");
     if (max_ctx < 0 || table_stride < 0 || max_ctx > table_stride * (int64_t)cfg_.block_size ||
@@ -959,6 +962,7 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType quer
     a.num_seqs = (int)num_seqs;
     a.kv_heads = (int)kv;
     a.group = (int)group;
+    a.q_len = (int)q_len;
     a.num_q_heads = (int)num_q_heads;
     a.layer_row0 = (int)(layer * (int64_t)(cfg_.num_blocks * cfg_.block_size));
     a.num_blocks = (int)cfg_.num_blocks;
@@ -973,7 +977,7 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType quer
     }
     a.err = d_err_;
     if (a.num_splits > 1) {
-        const size_t parts = (size_t)num_seqs * num_q_heads * a.num_splits;
+        const size_t parts = (size_t)num_seqs * q_len * num_q_heads * a.num_splits;
         const size_t need = parts * (hd + 1) * sizeof(float);
         if (need > d_attn_ws_bytes_) {
             // The old workspace may still be read by attention work in flight.

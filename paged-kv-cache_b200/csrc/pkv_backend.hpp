@@ -64,11 +64,13 @@ class B200Backend {
     Status set_copy_engine(int engine);
     Status set_kv_scales(const float *k_scales, const float *v_scales, uint64_t count);
     // query: the type of q and out; the pool dtype for bf16/f16 pools, bf16
-    // or f16 over an fp8 pool.
+    // or f16 over an fp8 pool. q_len: query tokens per sequence (the last
+    // q_len positions of its context, causal among themselves).
     Status paged_attention_dev(int64_t layer, const void *q, DType query, int64_t q_seq_stride,
                                int64_t num_seqs, int64_t num_q_heads, const int32_t *tables,
                                int64_t table_stride, const int32_t *ctx, int64_t max_ctx,
-                               float softmax_scale, void *out, float *lse, cudaStream_t s);
+                               float softmax_scale, void *out, float *lse, cudaStream_t s,
+                               int64_t q_len = 1);
     Status resolve_slots_dev(const int32_t *tables, int64_t table_stride, const int32_t *ctx,
                              const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
                              int32_t *cu, int64_t *slots, cudaStream_t s);

@@ -225,6 +225,22 @@ int pkv_paged_attention_typed_dev(pkv_backend *b, int64_t layer, const void *q, 
     });
 }
 
+int pkv_paged_attention_multi_dev(pkv_backend *b, int64_t layer, const void *q, int query_dtype,
+                                  int64_t q_len, int64_t q_token_stride, int64_t num_seqs,
+                                  int64_t num_q_heads, const int32_t *block_tables,
+                                  int64_t table_stride, const int32_t *context_lens,
+                                  int64_t max_context_len, float softmax_scale, void *out,
+                                  float *lse, void *stream) {
+    if (!b) return null_handle();
+    if (!valid_dtype(query_dtype)) return bad_dtype();
+    return guarded("pkv_paged_attention_multi_dev", [&] {
+        return b->impl->paged_attention_dev(layer, q, static_cast<pkv::DType>(query_dtype),
+                                            q_token_stride, num_seqs, num_q_heads, block_tables,
+                                            table_stride, context_lens, max_context_len,
+                                            softmax_scale, out, lse, as_stream(stream), q_len);
+    });
+}
+
 int pkv_set_copy_engine(pkv_backend *b, int engine) {
     if (!b) return null_handle();
     return guarded("pkv_set_copy_engine", [&] { return b->impl->set_copy_engine(engine); });

@@ -159,16 +159,19 @@ struct DigestRowsLaunch {
 // Decode attention over one layer of the pool (pkv_attention.cu): one query
 // token per sequence, GQA groups of `group` query heads per kv head.
 struct AttnLaunch {
-    const void *q;             // [num_seqs][num_q_heads][head_dim], row pitch q_seq_stride
-    long long q_seq_stride;    // elements
-    void *out;                 // [num_seqs][num_q_heads][head_dim], contiguous
-    float *lse;                // [num_seqs][num_q_heads] natural-log sum of exp, or null
+    const void *q;             // [num_seqs * q_len][num_q_heads][head_dim], row pitch q_seq_stride
+    long long q_seq_stride;    // elements between consecutive query tokens
+    void *out;                 // [num_seqs * q_len][num_q_heads][head_dim], contiguous
+    float *lse;                // [num_seqs * q_len][num_q_heads] natural-log sum of exp, or null
     const int *tables;         // [num_seqs][table_stride]
     long long table_stride;
     const int *ctx;            // [num_seqs] tokens in the cache per sequence
     int num_seqs;
     int kv_heads;              // kv heads held by this backend
-    int group;                 // query heads per kv head (<= 16)
+    int group;                 // query heads per kv head
+    // Query tokens per sequence (q_len * group <= 16): token i of sequence s
+    // sits at position ctx[s] - q_len + i and attends keys 0 .. that position.
+    int q_len = 1;
     int num_q_heads;           // kv_heads * group
     int layer_row0;            // layer * num_blocks * block_size: first pool row of the layer
     int num_blocks;
@@ -176,8 +179,8 @@ struct AttnLaunch {
     int blocks_per_split;
     int num_splits;
     float scale_log2;          // softmax scale * log2(e)
-    float *part_o;             // [num_seqs][num_q_heads][num_splits][head_dim] when num_splits > 1
-    float *part_lse;           // [num_seqs][num_q_heads][num_splits], base-2
+    float *part_o;             // [num_seqs * q_len][num_q_heads][num_splits][head_dim] when num_splits > 1
+    float *part_lse;           // [num_seqs * q_len][num_q_heads][num_splits], base-2
     // fp8 pools: dequantisation scales [num_layers][num_kv_heads] (device
     // memory) and the index of this layer's first kv head held here.
     const float *k_scale = nullptr;

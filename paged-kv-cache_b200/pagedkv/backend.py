@@ -256,27 +256,38 @@ class B200Backend:
 
     def paged_attention(self, q, block_tables, context_lens, max_context_len: int, out,
                         layer: int, softmax_scale: float | None = None, lse=None,
-                        stream=None) -> None:
-        """Decode attention over one layer (pkv_paged_attention_typed_dev): q
-        and out [num_seqs][num_q_heads][head_dim], bf16 or f16 (the pool
-        dtype, or either over an fp8 pool), block_tables int32
-        [num_seqs][stride], context_lens int32 [num_seqs], lse optional f32
-        [num_seqs][num_q_heads]."""
-        s, hq, d = q.shape
+                        stream=None, q_len: int = 1) -> None:
+        """Paged attention over one layer: q and out [num_seqs * q_len]
+        [num_q_heads][head_dim], bf16 or f16 (the pool dtype, or either over
+        an fp8 pool), block_tables int32 [num_seqs][stride], context_lens
+        int32 [num_seqs], lse optional f32 [num_seqs * q_len][num_q_heads].
+        q_len 1 is decode (pkv_paged_attention_typed_dev); q_len > 1 query
+        tokens per sequence are the last q_len positions of its context,
+        causal among themselves (pkv_paged_attention_multi_dev)."""
+        rows, hq, d = q.shape
+        if q_len < 1 or rows % q_len:
+            raise ValueError("q must hold q_len rows per sequence")
         if q.stride(2) != 1 or q.stride(1) != d:
             raise ValueError("q must hold contiguous [heads][head_dim] rows")
-        if not out.is_contiguous() or tuple(out.shape) != (s, hq, d):
-            raise ValueError("out must be a dense [num_seqs][num_q_heads][head_dim] tensor")
+        if not out.is_contiguous() or tuple(out.shape) != (rows, hq, d):
+            raise ValueError("out must be a dense [num_seqs * q_len][num_q_heads][head_dim] tensor")
         if out.dtype != q.dtype:
             raise ValueError("out must have the dtype of q")
         if softmax_scale is None:
             softmax_scale = d ** -0.5
         stride = block_tables.shape[1] if block_tables.dim() == 2 else 0
-        _check(lib.pkv_paged_attention_typed_dev(self._h, layer, _ptr(q), _torch_tag(q), q.stride(0),
-                                                 s, hq, _ptr(block_tables), stride,
-                                                 _ptr(context_lens), max_context_len,
-                                                 float(softmax_scale), _ptr(out), _ptr(lse),
-                                                 _stream_ptr(stream)))
+        if q_len == 1:
+            _check(lib.pkv_paged_attention_typed_dev(self._h, layer, _ptr(q), _torch_tag(q), q.stride(0),
+                                                     rows, hq, _ptr(block_tables), stride,
+                                                     _ptr(context_lens), max_context_len,
+                                                     float(softmax_scale), _ptr(out), _ptr(lse),
+                                                     _stream_ptr(stream)))
+        else:
+            _check(lib.pkv_paged_attention_multi_dev(self._h, layer, _ptr(q), _torch_tag(q), q_len,
+                                                     q.stride(0), rows // q_len, hq,
+                                                     _ptr(block_tables), stride, _ptr(context_lens),
+                                                     max_context_len, float(softmax_scale), _ptr(out),
+                                                     _ptr(lse), _stream_ptr(stream)))
 
     def digest(self, stream=None) -> tuple[int, int]:
         k, v = C.c_uint64(), C.c_uint64()
