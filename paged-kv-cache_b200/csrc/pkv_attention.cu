@@ -101,11 +101,11 @@ struct AttnGeom {
 // others' streaming.
 template <int D, bool FP8>
 __host__ __device__ constexpr int attn_stages(int nt) {
-    return (D <= 128 && nt == 1 && !FP8) ? 2 : 3;
+    return (D <= 128 && !FP8) ? 2 : 3;
 }
 template <int D, bool FP8>
 __host__ __device__ constexpr int attn_min_ctas(int nt) {
-    return D > 128 ? 2 : FP8 ? (nt == 1 ? 4 : 3) : (nt == 1 ? 3 : 2);
+    return D > 128 ? 2 : FP8 ? (nt == 1 ? 4 : 3) : 3;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
