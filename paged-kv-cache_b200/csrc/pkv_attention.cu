@@ -280,13 +280,16 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    pdl_wait();  // launched as a programmatic dependent of the previous grid (a layer's combine)
     const int ctx = checked_ctx(a, seq, threadIdx.x == 0 && split == 0 && kvh == 0);
     const int nblk = (ctx + kTok - 1) / kTok;
     const int b0 = split * a.blocks_per_split;
     const int b1 = min(nblk, b0 + a.blocks_per_split);
     // The combine kernel (launched as a programmatic dependent of this grid)
     // may be scheduled from here on; it waits for this grid's completion.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Without splits the next grid is another layer's attention, released
+    // only as this grid's CTAs exit.
+    if (a.num_splits > 1) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (split > 0 && b0 >= b1) return;  // beyond this sequence's splits: the combine skips it
 
     // Query tile: row r < cols is query token r / group (of the sequence's
@@ -810,8 +813,7 @@ cudaError_t launch_main(const AttnLaunch &a, const CUtensorMap *maps, cudaStream
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)a.num_splits, (unsigned)a.kv_heads, (unsigned)a.num_seqs);
-    kern<<<grid, kAttnThreads, G::kSmem, st>>>(maps[0], maps[1], a);
-    return cudaGetLastError();
+    return launch_pdl(kern, grid, dim3(kAttnThreads), G::kSmem, st, maps[0], maps[1], a);
 }
 
 template <typename T, int D, bool FP8>

@@ -249,6 +249,7 @@ __device__ __forceinline__ void resolve_cache_fp8_general(const ResolveCacheLaun
 template <typename S, int PER, int UNROLL, int MIN_CTAS>
 __global__ void __launch_bounds__(kThreads, MIN_CTAS)
 resolve_cache_fp8_kernel(ResolveCacheLaunch a, long long groups, int layers_per_chunk) {
+    pdl_wait();
     resolve_cache_fp8_general<S, PER, UNROLL>(a, groups, layers_per_chunk);
 }
 
@@ -268,6 +269,7 @@ __device__ __noinline__ void resolve_cache_fp8_general_call(ResolveCacheLaunch a
 template <typename S, int UNROLL>
 __global__ void __launch_bounds__(kThreads, 4)
 resolve_cache_fp8_decode_kernel(ResolveCacheLaunch a, long long groups, int layers_per_chunk) {
+    pdl_wait();
     const long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const bool active = it < a.num_tokens * groups;
     const int l0 = blockIdx.y * layers_per_chunk;
@@ -475,8 +477,7 @@ cudaError_t resolve_cache_fp8_s(const ResolveCacheLaunch &a, int sms, cudaStream
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    kern<<<grid, kThreads, smem, st>>>(a, groups, lpc);
-    return cudaGetLastError();
+    return launch_pdl(kern, grid, dim3(kThreads), smem, st, a, groups, lpc);
 }
 
 template <typename S>

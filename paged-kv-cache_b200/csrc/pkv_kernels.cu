@@ -432,6 +432,7 @@ __device__ __noinline__ void resolve_cache_general_call(ResolveCacheLaunch a, in
 template <typename V, int UNROLL, int MIN_CTAS>
 __global__ void __launch_bounds__(kThreads, MIN_CTAS)
 resolve_cache_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
+    pdl_wait();
     resolve_cache_general<V, UNROLL>(a, nvec, layers_per_chunk);
 }
 
@@ -445,6 +446,7 @@ resolve_cache_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
 template <typename V, int UNROLL>
 __global__ void __launch_bounds__(kThreads, 4)
 resolve_cache_decode_kernel(ResolveCacheLaunch a, int nvec, int layers_per_chunk) {
+    pdl_wait();
     const long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const bool active = it < a.num_tokens * nvec;
     const int l0 = blockIdx.y * layers_per_chunk;
@@ -832,8 +834,7 @@ cudaError_t resolve_cache_v(const ResolveCacheLaunch &a, long long entry_bytes, 
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    kern<<<grid, kThreads, smem, st>>>(a, nvec, lpc);
-    return cudaGetLastError();
+    return launch_pdl(kern, grid, dim3(kThreads), smem, st, a, nvec, lpc);
 }
 }  // namespace
 
