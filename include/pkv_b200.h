@@ -248,7 +248,14 @@ int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64
  * [num_seqs][num_q_heads]) receives log(sum exp(scale * q.k)); an empty
  * context gives a zero output and lse = -inf. Block ids outside the pool are
  * recorded (InvalidBlock) and their tokens skipped. softmax_scale must be
- * finite and positive. */
+ * finite and positive.
+ *
+ * Long contexts are split over several CTAs whose partial results live in a
+ * per-handle device workspace. A call that needs more workspace than every
+ * earlier call on the handle synchronises the device and allocates it
+ * (cudaMalloc), which a stream capture does not allow: run the largest shape
+ * once before capturing attention calls into a CUDA graph. The other
+ * device-pointer entry points allocate nothing per call. */
 int pkv_paged_attention_dev(pkv_backend *b, int64_t layer, const void *q, int64_t q_seq_stride,
                             int64_t num_seqs, int64_t num_q_heads, const int32_t *block_tables,
                             int64_t table_stride, const int32_t *context_lens,
