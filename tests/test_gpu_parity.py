@@ -651,6 +651,76 @@ def test_decode_form_of_the_fused_step_matches_the_general_form(cuda, case):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
+@pytest.mark.parametrize("form", ["decode", "general"])
+def test_consecutive_fused_steps_keep_stream_order(cuda, form):
+    """The fused step kernels are launched as programmatic dependents of the
+    previous grid in their stream and wait for it before touching memory.
+    Eight steps on one stream write the same slots: with a torch kernel
+    rewriting the source rows before each step (and a torch gather of the
+    written rows after it), every step must write the rows copied just before
+    it; back to back, eagerly and replayed from a CUDA graph, the pool must
+    end with the last step's rows."""
+    import torch
+
+    cfg = CacheConfig(1024, 16, 2, 64, 4, 2)
+    e, L = cfg.entry_elems(), cfg.num_layers
+    batch = decode_batch(seed=None, num_seqs=64, max_ctx=300, cfg=cfg)
+    tables, ctx, new = batch.tables.copy(), batch.ctx.copy(), batch.new.copy()
+    if form == "general":  # still one token per sequence on average: the scan runs
+        new[0], new[1] = 2, 0
+        need = -(-(ctx[0] + 2) // 16)
+        if tables[0, need - 1] < 0:
+            tables[0, need - 1] = int(np.setdiff1d(np.arange(cfg.num_blocks), tables)[0])
+    t, steps = int(new.sum()), 8
+    tab, dctx, dnew = (torch.from_numpy(x).to(cuda) for x in (tables, ctx, new))
+    g = torch.Generator(device=cuda).manual_seed(31)
+    src = torch.randn((steps, 2, L, t, e), generator=g, device=cuda).to(torch.bfloat16)
+    b = B200Backend(cfg, dtype="bf16")
+    cu = torch.empty(len(new) + 1, dtype=torch.int32, device=cuda)
+    sl = torch.empty(t, dtype=torch.int64, device=cuda)
+    b.resolve_and_cache(tab, dctx, dnew, t, cu, src[0, 0], src[0, 1], slots_out=sl)
+    torch.cuda.synchronize()
+    assert b.device_error() is None
+    kp, vp = (x.view(L, -1, e) for x in b.planes())
+
+    def rows():
+        return torch.stack([kp[:, sl], vp[:, sl]])
+
+    stream = torch.cuda.Stream()
+    k = torch.empty_like(src[0, 0])
+    v = torch.empty_like(src[0, 1])
+    snaps = []
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            k.copy_(src[i, 0])
+            v.copy_(src[i, 1])
+            b.resolve_and_cache(tab, dctx, dnew, t, cu, k, v, slots_out=sl, stream=stream)
+            snaps.append(rows())
+    stream.synchronize()
+    for i in range(steps):
+        assert torch.equal(snaps[i], src[i]), f"step {i}"
+    for order in (list(range(steps)), list(reversed(range(steps)))):
+        last = order[-1]
+        with torch.cuda.stream(stream):
+            for i in order:
+                b.resolve_and_cache(tab, dctx, dnew, t, cu, src[i, 0], src[i, 1], slots_out=sl,
+                                    stream=stream)
+        stream.synchronize()
+        assert torch.equal(rows(), src[last])
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            b.resolve_and_cache(tab, dctx, dnew, t, cu, src[i, 0], src[i, 1], slots_out=sl,
+                                stream=stream)
+    b.resolve_and_cache(tab, dctx, dnew, t, cu, src[0, 0], src[0, 1], slots_out=sl)
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(rows(), src[steps - 1])
+    assert b.device_error() is None
+    del graph
+
+
 def test_fused_resolve_and_cache_flags_bad_tables_and_writes_nothing_for_them(cuda):
     import torch
 
