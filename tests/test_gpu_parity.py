@@ -293,6 +293,41 @@ def test_device_reshape_per_layer_and_all_layers_match_oracle(cuda):
     assert_pools_equal(b, cpu)
 
 
+@pytest.mark.parametrize("tokens", [2000, 1150, 700])
+def test_all_layer_scatter_at_70b_geometry_equals_per_layer_calls(cuda, tokens):
+    """80 layers of 2 KiB entries (the churn trace's geometry), token counts
+    of its decode steps: the all-layer launch (several waves at 2 CTAs per
+    SM, every thread walking all 80 layers) must write the pool that 80
+    per-layer launches write, and every row must land at its slot."""
+    import torch
+
+    cfg = CacheConfig(200, 16, 8, 128, 80, 2)
+    e, L = cfg.entry_elems(), cfg.num_layers
+    st = Stream(tokens)
+    slots = st.permutation(cfg.num_blocks * cfg.block_size)[:tokens].astype(np.int64)
+    slots[3] = -1  # a padding token
+    g = torch.Generator(device=cuda).manual_seed(tokens)
+    k = torch.randn((L, tokens, e), generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn((L, tokens, e), generator=g, device=cuda).to(torch.bfloat16)
+    d_slots = torch.from_numpy(slots).to(cuda)
+    a = B200Backend(cfg, dtype="bf16")
+    a.reshape_and_cache(k, v, d_slots)
+    b = B200Backend(cfg, dtype="bf16")
+    for layer in range(L):
+        b.reshape_and_cache(k[layer], v[layer], d_slots, layer=layer)
+    torch.cuda.synchronize()
+    assert a.device_error() is None and b.device_error() is None
+    keep = torch.from_numpy(slots >= 0).to(cuda)
+    for pa, pb, src in zip(a.planes(), b.planes(), (k, v)):
+        assert torch.equal(pa.view(torch.int16), pb.view(torch.int16))
+        flat = pa.view(L, -1, e)
+        assert torch.equal(flat[:, d_slots[keep]], src[:, keep])
+        assert int(torch.count_nonzero(flat.view(torch.int16))) == int(keep.sum()) * L * e - int(
+            (src[:, keep].view(torch.int16) == 0).sum())
+    a.close()
+    b.close()
+
+
 def test_device_reshape_reads_strided_rows_and_converts(cuda):
     import torch
 
