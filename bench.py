@@ -58,6 +58,9 @@ def parse():
     p.add_argument("--graph-steps", type=int, default=0,
                    help="decode: steps captured per CUDA graph (0: the largest divisor of "
                         "--steps up to 8)")
+    p.add_argument("--strong", action="store_true",
+                   help="prefill/decode: strong scaling -- one chunk (or decode batch) over one "
+                        "32,768-block pool, head-sharded over the N GPUs, instead of N of them")
     p.add_argument("--unfused", action="store_true",
                    help="resolve slots and scatter in two launches instead of the fused kernel")
     p.add_argument("--pool-dtype", choices=["bf16", "fp8"], default="bf16",
@@ -356,11 +359,12 @@ def wl_table_batch(run, kind: str) -> dict:
     from pagedkv.shard import verify_over_group
 
     args, world, dev, stream = run.args, run.world, run.dev, run.stream
+    copies = 1 if args.strong else world  # chunks (decode batches) per step over all GPUs
     if kind == "prefill":
-        cfg, tables, ctx, new = build_batch(world, args.chunk_tokens, args.chunk_prompts,
+        cfg, tables, ctx, new = build_batch(copies, args.chunk_tokens, args.chunk_prompts,
                                             args.chunk_blocks)
     else:
-        cfg, tables, ctx, new = build_decode(world)
+        cfg, tables, ctx, new = build_decode(copies)
     T, S = int(new.sum()), len(new)
     fp8 = args.pool_dtype == "fp8"
     if fp8:
@@ -483,10 +487,10 @@ def wl_table_batch(run, kind: str) -> dict:
     # Every rank writes its head slice of all T tokens, so a step stores T
     # whole tokens across the N GPUs.
     if kind == "prefill":
-        workload = (f"ragged prefill chunk x{world}: {world}x{args.chunk_tokens} tokens ({S} prompts, "
+        workload = (f"ragged prefill chunk x{copies}: {copies}x{args.chunk_tokens} tokens ({S} prompts, "
                     "log-uniform 128..4096)")
     else:
-        workload = f"decode step x{world}: {world}x256 sequences, context U[1,4096], +1 token each"
+        workload = f"decode step x{copies}: {copies}x256 sequences, context U[1,4096], +1 token each"
     workload += (f", Qwen2-7B KV geometry (28 layers, 4 KV heads x 128, bs 16), pool "
                  f"{cfg.num_blocks} blocks (shuffled free list) head-sharded {world} ways, "
                  + ("fp8 E4M3 pool (bf16 rows quantised with per-layer, per-head scales)"
@@ -494,7 +498,8 @@ def wl_table_batch(run, kind: str) -> dict:
                  + ("device slot resolution + all-layer reshape_and_cache" if args.unfused else
                   "slot resolution fused with the all-layer reshape_and_cache (one launch)")
                  + (f" ({per_graph} steps captured per CUDA graph)" if graph is not None else ""))
-    out = base_line(run, T * K / (total_ms / 1e3), K, total_ms / K, "weak", workload, {
+    out = base_line(run, T * K / (total_ms / 1e3), K, total_ms / K,
+                    "strong" if args.strong else "weak", workload, {
         "tokens_per_step": T, "sequences_per_step": S, "layers": L, "entry_elems_per_gpu": es,
         "pool_gib_per_gpu": round(backend.allocated_bytes() / 2**30, 2),
         "parallelism": f"kv-head shards x{world}",
