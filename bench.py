@@ -915,8 +915,11 @@ def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks
     steps = max(1, min(args.steps, 5))
 
     def one():
+        # The step's destinations, built once and passed to every layer's call
+        # (a caller of the trait holds one slice of PhysicalSlots per step).
+        pairs = backend.slot_pairs(blocks, offs)
         for layer in range(L):
-            backend.write_kv_batch_slots(layer, blocks, offs, hk[layer], hv[layer], host_dtype="bf16")
+            backend.write_kv_batch_pairs(layer, pairs, hk[layer], hv[layer], host_dtype="bf16")
         if backend.device_error() is not None:
             raise SystemExit("device error in e2e step")
 

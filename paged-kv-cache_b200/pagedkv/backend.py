@@ -139,17 +139,30 @@ class B200Backend:
         _check(lib.pkv_write_kv_batch(self._h, layer, C.addressof(arr), len(dsts), ka.ctypes.data,
                                       ka.size, va.ctypes.data, va.size, tag))
 
-    def write_kv_batch_slots(self, layer: int, blocks: np.ndarray, slots: np.ndarray, k, v,
-                             host_dtype: str | None = None) -> None:
-        """write_kv_batch with the destinations given as two integer arrays."""
+    @staticmethod
+    def slot_pairs(blocks: np.ndarray, slots: np.ndarray) -> np.ndarray:
+        """Destinations as the C ABI's pkv_slot array ([n][2] uint64: block,
+        slot), built once and passed to every layer's write_kv_batch_pairs."""
         pairs = np.empty((len(blocks), 2), dtype=np.uint64)
         pairs[:, 0] = blocks
         pairs[:, 1] = slots
+        return pairs
+
+    def write_kv_batch_pairs(self, layer: int, pairs: np.ndarray, k, v,
+                             host_dtype: str | None = None) -> None:
+        """write_kv_batch with the destinations as a slot_pairs array."""
+        if pairs.dtype != np.uint64 or pairs.ndim != 2 or pairs.shape[1] != 2 or not pairs.flags.c_contiguous:
+            raise ValueError("pairs must be a contiguous [n][2] uint64 array (see slot_pairs)")
         tag = None if host_dtype is None else DTYPE_TAGS[host_dtype]
         ka, tag = _host_array(k, tag)
         va, _ = _host_array(v, tag)
-        _check(lib.pkv_write_kv_batch(self._h, layer, pairs.ctypes.data, len(blocks),
+        _check(lib.pkv_write_kv_batch(self._h, layer, pairs.ctypes.data, len(pairs),
                                       ka.ctypes.data, ka.size, va.ctypes.data, va.size, tag))
+
+    def write_kv_batch_slots(self, layer: int, blocks: np.ndarray, slots: np.ndarray, k, v,
+                             host_dtype: str | None = None) -> None:
+        """write_kv_batch with the destinations given as two integer arrays."""
+        self.write_kv_batch_pairs(layer, self.slot_pairs(blocks, slots), k, v, host_dtype)
 
     def read_kv(self, layer: int, src, k_out: np.ndarray, v_out: np.ndarray) -> None:
         """backend.rs:82-88: fills k_out and v_out (f32, f16, or uint16 = bf16 bits)."""
