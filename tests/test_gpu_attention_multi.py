@@ -86,6 +86,25 @@ def test_fp8_multi_query_matches_oracle(cuda, head_dim, q_len, group):
     check_multi(kp, vp, q, out, lse, tables, ctx, 0, q_len, None, TOL["bf16"])
 
 
+@pytest.mark.parametrize("q_len,group", [(3, 5), (2, 4)])
+def test_fp8_multi_query_with_f16_queries(cuda, q_len, group):
+    """f16 queries over an fp8 pool (held to the f16 tolerance), the 16-row
+    and the 8-row form."""
+    import torch
+
+    cfg, b, ks, vs = setup_fp8(cuda, head_dim=128, num_blocks=900, seed=40 + q_len)
+    st = Stream(900 + q_len)
+    ctx = np.array([max(c, q_len) for c in CTX])
+    tables = tables_for(st, cfg, ctx)
+    hq = cfg.num_kv_heads * group
+    q_np = st.normal(len(ctx) * q_len * hq * 128).reshape(len(ctx) * q_len, hq,
+                                                          128).astype(np.float32)
+    q, out, lse = run_multi(cuda, b, torch.float16, q_np, tables, ctx, int(ctx.max()), 1, q_len)
+    assert b.device_error() is None
+    kp, vp = dequantised(b, ks, vs, 128)
+    check_multi(kp, vp, q, out, lse, tables, ctx, 1, q_len, None, TOL["f16"])
+
+
 def test_one_token_through_the_multi_entry_is_decode(cuda):
     """q_len 1 on pkv_paged_attention_multi_dev gives decode's bits."""
     import ctypes as C
