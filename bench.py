@@ -74,6 +74,8 @@ def parse():
     p.add_argument("--q-len", type=int, default=1,
                    help="attention: query tokens per sequence (the last q_len positions, causal; "
                         "q_len * 7 <= 16)")
+    p.add_argument("--no-plan", action="store_true",
+                   help="attention: sequences in batch order (no pkv_paged_attention_plan_dev)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-ops", action="store_true")
@@ -631,10 +633,14 @@ def wl_attention(run) -> dict:
     out = torch.empty((L, S * ql, hq, D), dtype=torch.bfloat16, device=dev)
     lse = torch.empty((L, S * ql, hq), dtype=torch.float32, device=dev)
 
+    plan = not args.no_plan  # one longest-first order per step, for all its layers
+
     def step(i, ev):
         if ev is not None:
             ev.extend(torch.cuda.Event(enable_timing=True) for _ in range(2))
             ev[0].record(stream)
+        if plan:
+            backend.paged_attention_plan(d_len, max_ctx, stream=stream)
         for l in range(L):
             backend.paged_attention(q, d_tab, d_len, max_ctx, out[l], l, lse=lse[l], stream=stream,
                                     q_len=ql)
@@ -675,6 +681,8 @@ def wl_attention(run) -> dict:
         # and tensor maps exist already after the warm-up).
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
+            if plan:
+                backend.paged_attention_plan(d_len, max_ctx, stream=stream)
             for l in range(L):
                 backend.paged_attention(q, d_tab, d_len, max_ctx, out[l], l, lse=lse[l], stream=stream,
                                         q_len=ql)
@@ -698,7 +706,9 @@ def wl_attention(run) -> dict:
                 f"(mean {lens.mean():.0f}), Qwen2-7B (28 query heads over 4 kv heads x 128, "
                 f"{L} layers, bs 16, bf16 queries), pool {cfg.num_blocks} blocks "
                 + ("of E4M3 codes with per-(layer, kv head) scales" if fp8 else "bf16")
-                + f" head-sharded {world} ways; step = paged attention over every layer"
+                + f" head-sharded {world} ways; step = "
+                + ("a longest-first order of the sequences (one plan kernel), then " if plan else "")
+                + "paged attention over every layer"
                 + (f" with its last {ql} tokens as causal query tokens" if ql > 1 else "")
                 + (" replayed as one CUDA graph" if graph is not None else ""))
     out_line = base_line(run, int(lens.sum()) * world * K / (total_ms / 1e3), K, total_ms / K,
@@ -715,7 +725,7 @@ def wl_attention(run) -> dict:
     out_line["unit"] = "tokens/s"
     out_line["gb_per_s"] = alg * world / (total_ms / K / 1e3) / 1e9
     out_line["roofline"] = roofline(f"paged_attention_kernel + combine ({L} layers)", alg, kernel_ms)
-    out_line["gpu_launches"] = K * L * 2
+    out_line["gpu_launches"] = K * (L * 2 + (1 if plan else 0))
     out_line["spot_check_max_abs_err"] = worst
     out_line["config"]["pool_dtype"] = "fp8_e4m3" if fp8 else "bf16"
     out_line["config"]["q_len"] = ql

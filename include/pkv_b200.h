@@ -291,6 +291,20 @@ int pkv_paged_attention_multi_dev(pkv_backend *b, int64_t layer, const void *q, 
                                   int64_t max_context_len, float softmax_scale, void *out,
                                   float *lse, void *stream);
 
+/* Schedule for the paged attention calls that follow (a decode step's
+ * layers): reads context_lens on the device and orders the sequences by
+ * descending length, so that each layer's grid starts with its long
+ * sequences and ends with its short ones instead of waiting on a long one
+ * that happened to come last. Later pkv_paged_attention_dev / _typed_dev /
+ * _multi_dev calls on this handle with the same context_lens pointer,
+ * num_seqs and max_context_len use it; other calls run in launch order. The
+ * plan only schedules: the results are the same bit for bit, also when
+ * context_lens has changed since, so plan once per step after the lengths
+ * are written. The first plan on a handle allocates 256 KiB of device
+ * memory. No counterpart in the reference. */
+int pkv_paged_attention_plan_dev(pkv_backend *b, const int32_t *context_lens, int64_t num_seqs,
+                                 int64_t max_context_len, void *stream);
+
 /* Order-independent 64-bit digests of this backend's K and V planes (the
  * element's global index in the full plane and its f32-widened bits, summed;
  * zeros contribute nothing). Digests of the shards of one pool add up

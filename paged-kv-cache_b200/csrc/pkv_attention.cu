@@ -279,8 +279,15 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
     unsigned char *qs = smem + kAttnWarps * G::kRingBytes;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    const int split = blockIdx.x, kvh = blockIdx.y;
     pdl_wait();  // launched as a programmatic dependent of the previous grid (a layer's combine)
+    // With a plan, grid slot z (dispatched in z order) takes the sequence
+    // the plan put there, the longest first.
+    int seq = blockIdx.z;
+    if (a.order) {
+        seq = (int)__ldg(a.order + blockIdx.z);
+        if (seq >= a.num_seqs) return;  // not a sequence (a plan made while the lengths changed)
+    }
     const int ctx = checked_ctx(a, seq, threadIdx.x == 0 && split == 0 && kvh == 0);
     const int nblk = (ctx + kTok - 1) / kTok;
     const int b0 = split * a.blocks_per_split;
@@ -891,6 +898,53 @@ cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long
         if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
     }
     return cudaSuccess;
+}
+
+namespace {
+// One CTA: counting sort of the sequences by block count, largest first
+// (counts above kPlanKeys - 1 share a bucket after a right shift).
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanKeys = 4096;
+__global__ void __launch_bounds__(kPlanThreads)
+attention_plan_kernel(const int *__restrict__ ctx, int num_seqs, int max_ctx, int shift,
+                      unsigned *__restrict__ order) {
+    __shared__ unsigned s_count[kPlanKeys];
+    pdl_wait();
+    for (int k = threadIdx.x; k < kPlanKeys; k += kPlanThreads) s_count[k] = 0;
+    __syncthreads();
+    auto key = [&](int s) {
+        const int c = __ldg(ctx + s);
+        const int nblk = (c < 0 || c > max_ctx) ? 0 : (c + kTok - 1) / kTok;
+        return min(kPlanKeys - 1, nblk >> shift);
+    };
+    for (int s = threadIdx.x; s < num_seqs; s += kPlanThreads) atomicAdd(&s_count[key(s)], 1u);
+    __syncthreads();
+    if (threadIdx.x == 0) {  // bucket starts, descending keys
+        unsigned at = 0;
+        for (int k = kPlanKeys - 1; k >= 0; --k) {
+            const unsigned n = s_count[k];
+            s_count[k] = at;
+            at += n;
+        }
+    }
+    __syncthreads();
+    // The lengths are read again here; should a caller rewrite them while
+    // this runs, positions past the end are dropped rather than written.
+    for (int s = threadIdx.x; s < num_seqs; s += kPlanThreads) {
+        const unsigned pos = atomicAdd(&s_count[key(s)], 1u);
+        if (pos < (unsigned)num_seqs) order[pos] = (unsigned)s;
+    }
+}
+}  // namespace
+
+cudaError_t launch_attention_plan(const int *ctx, int num_seqs, int max_ctx, unsigned *order,
+                                  cudaStream_t st) {
+    if (num_seqs <= 0) return cudaSuccess;
+    const int max_blocks = (max_ctx + kTok - 1) / kTok;
+    int shift = 0;
+    while ((max_blocks >> shift) >= kPlanKeys) ++shift;
+    return launch_pdl(attention_plan_kernel, dim3(1), dim3(kPlanThreads), 0, st, ctx, num_seqs, max_ctx,
+                      shift, order);
 }
 
 int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split) {

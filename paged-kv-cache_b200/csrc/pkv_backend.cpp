@@ -220,6 +220,7 @@ B200Backend::~B200Backend() {
     if (d_err_) cudaFree(d_err_);
     if (d_inv_) cudaFree(d_inv_);
     if (d_attn_ws_) cudaFree(d_attn_ws_);
+    if (d_plan_) cudaFree(d_plan_);
     if (d_stage_) cudaFree(d_stage_);
     if (h_stage_) cudaFreeHost(h_stage_);
     if (h_stage_free_) cudaEventDestroy(h_stage_free_);
@@ -976,6 +977,7 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType quer
         a.scale_row = layer * (long long)cfg_.num_kv_heads + (long long)(elem_offset() / hd);
     }
     a.err = d_err_;
+    if (d_plan_ && plan_ctx_ == ctx && plan_seqs_ == num_seqs && plan_max_ctx_ == max_ctx) a.order = d_plan_;
     if (a.num_splits > 1) {
         const size_t parts = (size_t)num_seqs * q_len * num_q_heads * a.num_splits;
         const size_t need = parts * (hd + 1) * sizeof(float);
@@ -994,6 +996,29 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType quer
         a.part_lse = d_attn_ws_ + parts * hd;
     }
     return check("paged_attention", launch_paged_attention(a, tmaps_, dtype_, query, (int)hd, st));
+}
+
+Status B200Backend::paged_attention_plan_dev(const int32_t *ctx, int64_t num_seqs, int64_t max_ctx,
+                                             cudaStream_t st) {
+    plan_ctx_ = nullptr;  // no plan unless this one is made
+    if (num_seqs < 0 || num_seqs > 65535)
+        return error(PKV_ERR_DEVICE, 0, 0, "at most 65535 sequences per call");
+    if (max_ctx < 0 || max_ctx > std::numeric_limits<int32_t>::max() - 16)
+        return error(PKV_ERR_SHAPE_MISMATCH, 0, max_ctx, "max_context_len out of range");
+    if (num_seqs == 0) return Status::Ok();
+    if (!ctx) return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    DeviceGuard g(device_);
+    cudaError_t e;
+    if (!d_plan_ && (e = cudaMalloc(&d_plan_, 65536 * sizeof(unsigned))) != cudaSuccess) {
+        d_plan_ = nullptr;
+        return device_error("allocating the attention plan", e);
+    }
+    if ((e = launch_attention_plan(ctx, (int)num_seqs, (int)max_ctx, d_plan_, st)) != cudaSuccess)
+        return check("paged_attention_plan", e);
+    plan_ctx_ = ctx;
+    plan_seqs_ = num_seqs;
+    plan_max_ctx_ = max_ctx;
+    return Status::Ok();
 }
 
 Status B200Backend::digest(uint64_t *k, uint64_t *v, cudaStream_t st) {

@@ -71,6 +71,9 @@ class B200Backend {
                                int64_t table_stride, const int32_t *ctx, int64_t max_ctx,
                                float softmax_scale, void *out, float *lse, cudaStream_t s,
                                int64_t q_len = 1);
+    // Longest-first order of the sequences for the attention calls that
+    // follow with the same ctx buffer, num_seqs and max_ctx (scheduling only).
+    Status paged_attention_plan_dev(const int32_t *ctx, int64_t num_seqs, int64_t max_ctx, cudaStream_t s);
     Status resolve_slots_dev(const int32_t *tables, int64_t table_stride, const int32_t *ctx,
                              const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
                              int32_t *cu, int64_t *slots, cudaStream_t s);
@@ -159,6 +162,11 @@ class B200Backend {
     bool tmaps_ready_ = false;
     float *d_attn_ws_ = nullptr;
     size_t d_attn_ws_bytes_ = 0;
+    // The attention plan (sequence order, 65,535 entries) and the call shape
+    // it was made for.
+    unsigned *d_plan_ = nullptr;
+    const int32_t *plan_ctx_ = nullptr;
+    int64_t plan_seqs_ = -1, plan_max_ctx_ = -1;
     std::string gpu_name_;
 };
 

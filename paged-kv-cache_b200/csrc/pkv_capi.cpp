@@ -241,6 +241,15 @@ int pkv_paged_attention_multi_dev(pkv_backend *b, int64_t layer, const void *q, 
     });
 }
 
+int pkv_paged_attention_plan_dev(pkv_backend *b, const int32_t *context_lens, int64_t num_seqs,
+                                 int64_t max_context_len, void *stream) {
+    if (!b) return null_handle();
+    return guarded("pkv_paged_attention_plan_dev", [&] {
+        return b->impl->paged_attention_plan_dev(context_lens, num_seqs, max_context_len,
+                                                 as_stream(stream));
+    });
+}
+
 int pkv_set_copy_engine(pkv_backend *b, int engine) {
     if (!b) return null_handle();
     return guarded("pkv_set_copy_engine", [&] { return b->impl->set_copy_engine(engine); });

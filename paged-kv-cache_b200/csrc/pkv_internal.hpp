@@ -186,6 +186,9 @@ struct AttnLaunch {
     const float *k_scale = nullptr;
     const float *v_scale = nullptr;
     long long scale_row = 0;
+    // Optional order of the sequences (pkv_paged_attention_plan_dev): grid
+    // slot z runs sequence order[z]. Any permutation gives the same results.
+    const unsigned *order = nullptr;
     DevError *err;
 };
 
@@ -212,6 +215,11 @@ cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long
                                  long long rows, int head_dim,
                                  void *tmaps_out /* 2 x 128 bytes, 64-aligned */);
 int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split);
+// The sequences ordered by descending block count (ctx entries outside
+// [0, max_ctx] count as empty, as the attention kernel treats them):
+// order[num_seqs].
+cudaError_t launch_attention_plan(const int *ctx, int num_seqs, int max_ctx, unsigned *order,
+                                  cudaStream_t s);
 // pool: the pool dtype; query: the type of q and out (the pool dtype for
 // bf16/f16 pools; bf16 or f16 over an fp8 pool).
 cudaError_t launch_paged_attention(const AttnLaunch &a, const void *tmaps, DType pool, DType query,

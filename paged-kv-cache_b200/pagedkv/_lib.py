@@ -72,6 +72,7 @@ _PROTOS = {
                                            C.c_float, _P, _P, _P]),
     "pkv_paged_attention_multi_dev": (_I, [_P, _I64, _P, _I, _I64, _I64, _I64, _I64, _P, _I64, _P,
                                            _I64, C.c_float, _P, _P, _P]),
+    "pkv_paged_attention_plan_dev": (_I, [_P, _P, _I64, _I64, _P]),
     "pkv_resolve_slots_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P]),
     "pkv_resolve_and_cache_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P, _P,
                                        _I64, _I64, _I, _P]),

@@ -267,6 +267,13 @@ class B200Backend:
                                              _ptr(slots_out), lay, _ptr(k), _ptr(v), tok_stride,
                                              layer_stride, tag, _stream_ptr(stream)))
 
+    def paged_attention_plan(self, context_lens, max_context_len: int, stream=None) -> None:
+        """Longest-first order of the sequences for the following
+        paged_attention calls with these context_lens
+        (pkv_paged_attention_plan_dev); results unchanged."""
+        _check(lib.pkv_paged_attention_plan_dev(self._h, _ptr(context_lens), context_lens.shape[0],
+                                                max_context_len, _stream_ptr(stream)))
+
     def paged_attention(self, q, block_tables, context_lens, max_context_len: int, out,
                         layer: int, softmax_scale: float | None = None, lse=None,
                         stream=None, q_len: int = 1) -> None:
