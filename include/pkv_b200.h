@@ -25,11 +25,12 @@
  * work on the handle's own blocking CUDA stream, which is ordered with the
  * legacy default stream; device entry points use the stream they are given.
  * Per-handle device state is shared by the calls that use it: the device
- * error word (all entry points) and the split workspace of
- * pkv_paged_attention_dev. Calls on one handle that run concurrently on
- * different streams share them too, so give one handle's device calls one
- * stream (or order the streams) when the error word or attention's
- * partial results must stay apart.
+ * error word (all entry points), the split workspace of the attention entry
+ * points and the sequence order of pkv_paged_attention_plan_dev. Calls on
+ * one handle that run concurrently on different streams share them too, so
+ * give one handle's device calls one stream (or order the streams) when the
+ * error word or attention's partial results must stay apart; a plan made on
+ * another stream while attention runs changes only the schedule.
  */
 #ifndef PKV_B200_H
 #define PKV_B200_H
