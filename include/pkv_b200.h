@@ -29,8 +29,9 @@
  * points and the sequence order of pkv_paged_attention_plan_dev. Calls on
  * one handle that run concurrently on different streams share them too, so
  * give one handle's device calls one stream (or order the streams) when the
- * error word or attention's partial results must stay apart; a plan made on
- * another stream while attention runs changes only the schedule.
+ * error word or attention's partial results must stay apart, and do not
+ * remake a plan while attention calls that read it run on another stream
+ * (they could read a mix of the two orders and skip a sequence).
  */
 #ifndef PKV_B200_H
 #define PKV_B200_H
