@@ -902,36 +902,61 @@ cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long
 
 namespace {
 // One CTA: counting sort of the sequences by block count, largest first
-// (counts above kPlanKeys - 1 share a bucket after a right shift).
+// (counts above kPlanKeys - 1 share a bucket after a right shift). Each
+// thread owns kPlanKeys / kPlanThreads consecutive buckets of the descending
+// key order, so the bucket starts are one block-wide exclusive scan.
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanKeys = 4096;
+constexpr int kPlanPer = kPlanKeys / kPlanThreads;
 __global__ void __launch_bounds__(kPlanThreads)
 attention_plan_kernel(const int *__restrict__ ctx, int num_seqs, int max_ctx, int shift,
                       unsigned *__restrict__ order) {
-    __shared__ unsigned s_count[kPlanKeys];
+    __shared__ unsigned s_count[kPlanKeys];  // indexed by descending key: kPlanKeys - 1 - key
+    __shared__ unsigned s_warp[kPlanThreads / 32];
     pdl_wait();
     for (int k = threadIdx.x; k < kPlanKeys; k += kPlanThreads) s_count[k] = 0;
     __syncthreads();
-    auto key = [&](int s) {
+    auto slot = [&](int s) {
         const int c = __ldg(ctx + s);
         const int nblk = (c < 0 || c > max_ctx) ? 0 : (c + kTok - 1) / kTok;
-        return min(kPlanKeys - 1, nblk >> shift);
+        return kPlanKeys - 1 - min(kPlanKeys - 1, nblk >> shift);
     };
-    for (int s = threadIdx.x; s < num_seqs; s += kPlanThreads) atomicAdd(&s_count[key(s)], 1u);
+    for (int s = threadIdx.x; s < num_seqs; s += kPlanThreads) atomicAdd(&s_count[slot(s)], 1u);
     __syncthreads();
-    if (threadIdx.x == 0) {  // bucket starts, descending keys
-        unsigned at = 0;
-        for (int k = kPlanKeys - 1; k >= 0; --k) {
-            const unsigned n = s_count[k];
-            s_count[k] = at;
-            at += n;
+    // Exclusive scan of the counts in slot order (descending keys).
+    unsigned c[kPlanPer], sum = 0;
+#pragma unroll
+    for (int i = 0; i < kPlanPer; ++i) sum += (c[i] = s_count[threadIdx.x * kPlanPer + i]);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned x = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        unsigned w = s_warp[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
         }
+        s_warp[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    unsigned at = x - sum + (warp > 0 ? s_warp[warp - 1] : 0u);
+#pragma unroll
+    for (int i = 0; i < kPlanPer; ++i) {
+        s_count[threadIdx.x * kPlanPer + i] = at;
+        at += c[i];
     }
     __syncthreads();
     // The lengths are read again here; should a caller rewrite them while
     // this runs, positions past the end are dropped rather than written.
     for (int s = threadIdx.x; s < num_seqs; s += kPlanThreads) {
-        const unsigned pos = atomicAdd(&s_count[key(s)], 1u);
+        const unsigned pos = atomicAdd(&s_count[slot(s)], 1u);
         if (pos < (unsigned)num_seqs) order[pos] = (unsigned)s;
     }
 }
