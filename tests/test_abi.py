@@ -53,6 +53,23 @@ def test_null_handle_is_a_device_error_not_a_crash():
     assert code == 9 and "null" in msg
 
 
+@pytest.mark.parametrize("name", [
+    "pkv_reshape_and_cache_dev", "pkv_copy_blocks_dev", "pkv_zero_blocks_dev",
+    "pkv_resolve_slots_dev", "pkv_resolve_and_cache_dev", "pkv_paged_attention_dev",
+    "pkv_paged_attention_typed_dev", "pkv_paged_attention_multi_dev",
+    "pkv_paged_attention_plan_dev", "pkv_digest", "pkv_digest_rows_dev"])
+def test_device_entry_points_reject_a_null_handle(name):
+    """Every device entry point checks its handle first (status 9, Device)."""
+    from pagedkv import _lib
+
+    f = getattr(_lib.lib, name)
+    args = [None if t in (C.c_void_p, C.c_char_p) or hasattr(t, "contents") else
+            (0.0 if t in (C.c_float, C.c_double) else 0) for t in f.argtypes]
+    assert f(*args) == 9
+    code, _, _, msg = _lib.last_error()
+    assert code == 9 and "null" in msg
+
+
 def test_unknown_dtype_tag_is_rejected_before_any_device_work():
     from pagedkv import _lib
 
