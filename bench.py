@@ -486,30 +486,11 @@ def wl_table_batch(run, kind: str) -> dict:
     if not verify["ok"]:
         raise SystemExit(f"bench: shard verification failed: {verify}")
 
-    # Every rank writes its head slice of all T tokens, so a step stores T
-    # whole tokens across the N GPUs.
-    if kind == "prefill":
-        workload = (f"ragged prefill chunk x{copies}: {copies}x{args.chunk_tokens} tokens ({S} prompts, "
-                    "log-uniform 128..4096)")
-    else:
-        workload = f"decode step x{copies}: {copies}x256 sequences, context U[1,4096], +1 token each"
-    workload += (f", Qwen2-7B KV geometry (28 layers, 4 KV heads x 128, bs 16), pool "
-                 f"{cfg.num_blocks} blocks (shuffled free list) head-sharded {world} ways, "
-                 + ("fp8 E4M3 pool (bf16 rows quantised with per-layer, per-head scales)"
-                    if fp8 else "bf16 pool") + "; step = "
-                 + ("device slot resolution + all-layer reshape_and_cache" if args.unfused else
-                  "slot resolution fused with the all-layer reshape_and_cache (one launch)")
-                 + (f" ({per_graph} steps captured per CUDA graph)" if graph is not None else ""))
+    workload, extra = table_batch_config(args, kind, world, cfg, T, S,
+                                         per_graph if graph is not None else 0)
     out = base_line(run, T * K / (total_ms / 1e3), K, total_ms / K,
-                    "strong" if args.strong else "weak", workload, {
-        "tokens_per_step": T, "sequences_per_step": S, "layers": L, "entry_elems_per_gpu": es,
-        "pool_gib_per_gpu": round(backend.allocated_bytes() / 2**30, 2),
-        "parallelism": f"kv-head shards x{world}",
-        "l2": ("inputs (K/V %.2f GiB per GPU) exceed the 126 MB L2; no flush needed"
-               % (2 * L * T * eb / 2**30)) if 2 * L * T * eb > 2**28 else
-              "inputs (%.1f MiB) fit in L2; every step rewrites the same rows, as a decode "
-              "step re-reads a projection's fresh output" % (2 * L * T * eb / 2**20),
-    }, "synthetic (seeded: shuffled free list, " + ("log-uniform prompt lengths" if kind == "prefill"
+                    "strong" if args.strong else "weak", workload, extra,
+                    "synthetic (seeded: shuffled free list, " + ("log-uniform prompt lengths" if kind == "prefill"
                                                        else "uniform context lengths") + ", normal K/V)")
     out["gb_per_s"] = alg_bytes * world / (total_ms / K / 1e3) / 1e9
     if fp8:
@@ -523,7 +504,6 @@ def wl_table_batch(run, kind: str) -> dict:
         prof = "reshape_prefill_ncu" if args.unfused else "resolve_cache_prefill_ncu"
     out["roofline"] = roofline(kname, alg_bytes, kernel_ms,
                                profile_traffic(prof) if kind == "prefill" else None)
-    out["config"]["pool_dtype"] = "fp8_e4m3" if fp8 else "bf16"
     if args.unfused:
         out["resolve_slots_ms"] = resolve_ms
     out["gpu_launches"] = (2 if args.unfused else 1) * K
@@ -533,7 +513,18 @@ def wl_table_batch(run, kind: str) -> dict:
     out["verify"] = verify
     out["clocks"] = clocks
     if kind == "prefill" and not args.no_ops and run.rank == 0:
-        out["ops"] = bench_ops(backend, cfg, dev, stream)
+        ops = bench_ops(backend, cfg, dev, stream)
+        cb = ops["copy_blocks"]
+        # The second kernel the metric names, as its own roofline object:
+        # the copy-on-write microbenchmark (distinct pairs, L2 flushed).
+        out["copy_blocks"] = {
+            **roofline("copy_blocks_kernel (256 distinct pairs x 28 layers x K,V planes of "
+                       f"{cfg.block_size * es * 2 // 1024} KiB, L2 flushed before each launch)",
+                       cb["algorithmic_bytes"], cb["ms"],
+                       profile_traffic("copy_blocks_pairs_ncu") if world == 1 else None),
+            "pairs": cb["pairs"], "layers": L, "launches_timed": cb["launches"]}
+        out["ops"] = {name: {"ms": round(r["ms"], 4), "frac": round(r["frac_of_peak"], 3)}
+                      for name, r in ops.items()}
     if not args.no_e2e:
         out["e2e"] = e2e_host_path(args, backend, tables, ctx, new, k, v, run.barrier,
                                    run.max_over_ranks)
@@ -545,7 +536,46 @@ def wl_table_batch(run, kind: str) -> dict:
                                          fp8_scales=(sk, sv) if fp8 else None)
     graph = None  # release the captured graph before its pool is freed
     backend.close()
+    if "copy_blocks" in out:  # last, so that a truncated tail of the line still holds it
+        out["copy_blocks"] = out.pop("copy_blocks")
     return out
+
+
+def table_batch_config(args, kind: str, world: int, cfg, T: int, S: int,
+                       per_graph: int = 0) -> tuple[str, dict]:
+    """`config.workload` and the other config keys of a prefill-chunk or
+    decode-step line. Both arms print the same ones: the reference arm
+    describes its bounded sample under `cpu_baseline.sample`."""
+    copies = 1 if args.strong else world
+    fp8 = args.pool_dtype == "fp8"
+    L = cfg.num_layers
+    es = cfg.num_kv_heads * cfg.head_dim // world
+    eb = es * 2
+    # Every rank writes its head slice of all T tokens, so a step stores T
+    # whole tokens across the N GPUs.
+    if kind == "prefill":
+        workload = (f"ragged prefill chunk x{copies}: {copies}x{args.chunk_tokens} tokens ({S} prompts, "
+                    "log-uniform 128..4096)")
+    else:
+        workload = f"decode step x{copies}: {copies}x256 sequences, context U[1,4096], +1 token each"
+    workload += (f", Qwen2-7B KV geometry (28 layers, 4 KV heads x 128, bs 16), pool "
+                 f"{cfg.num_blocks} blocks (shuffled free list) head-sharded {world} ways, "
+                 + ("fp8 E4M3 pool (bf16 rows quantised with per-layer, per-head scales)"
+                    if fp8 else "bf16 pool") + "; step = "
+                 + ("device slot resolution + all-layer reshape_and_cache" if args.unfused else
+                  "slot resolution fused with the all-layer reshape_and_cache (one launch)")
+                 + (f" ({per_graph} steps captured per CUDA graph)" if per_graph else ""))
+    pool_bytes = 2 * L * cfg.num_blocks * cfg.block_size * es * (1 if fp8 else 2)
+    return workload, {
+        "tokens_per_step": T, "sequences_per_step": S, "layers": L, "entry_elems_per_gpu": es,
+        "pool_gib_per_gpu": round(pool_bytes / 2**30, 2),
+        "parallelism": f"kv-head shards x{world}",
+        "l2": ("inputs (K/V %.2f GiB per GPU) exceed the 126 MB L2; no flush needed"
+               % (2 * L * T * eb / 2**30)) if 2 * L * T * eb > 2**28 else
+              "inputs (%.1f MiB) fit in L2; every step rewrites the same rows, as a decode "
+              "step re-reads a projection's fresh output" % (2 * L * T * eb / 2**20),
+        "pool_dtype": "fp8_e4m3" if fp8 else "bf16",
+    }
 
 
 def build_decode(world: int):
@@ -997,7 +1027,7 @@ def bench_ops(backend, cfg, dev, stream, reps: int = 10) -> dict:
         ms = sum(times) / len(times)
         gbs = nbytes / (ms / 1e3) / 1e9
         res[name] = {"ms": ms, "gb_per_s": gbs, "frac_of_peak": gbs / peak,
-                     "algorithmic_bytes": nbytes, **(extra or {})}
+                     "algorithmic_bytes": nbytes, "launches": len(times), **(extra or {})}
 
     pairs = torch.from_numpy(np.stack([ids[:256], ids[256:512]], 1).astype(np.int64)).to(dev)
     timed(lambda: backend.copy_blocks_dev(pairs, stream=stream),
@@ -1104,14 +1134,20 @@ def cpu_sample(tables, ctx, new, kf, vf, seconds: float, threads: int, head_dim=
 def run_reference(args):
     """The reference algorithm on the host cores: CpuBackend semantics
     (oracle/pkv_oracle.c; the Rust crate cannot be built here), one thread
-    per core over disjoint tokens, on a bounded sample of the same workload."""
+    per core over disjoint tokens, on a bounded sample of the same workload.
+    The reference's CpuBackend itself is single-threaded (cpu.rs:95-111): the
+    line also carries that figure, measured on the same sample. Nothing here
+    loads the device library."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     from pagedkv.workloads import Stream, bf16_bits_to_f32, f32_to_bf16_bits
 
-    cfg, tables, ctx, new = build_batch(1)
+    copies = 1 if args.strong else world
+    cfg, tables, ctx, new = build_batch(copies, args.chunk_tokens, args.chunk_prompts,
+                                        args.chunk_blocks)
+    workload, extra = table_batch_config(args, "prefill", world, cfg, int(new.sum()), len(new))
     L = cfg.num_layers
     threads = os.cpu_count() or 1
     sample = 4096
@@ -1127,14 +1163,19 @@ def run_reference(args):
             times.append(time.perf_counter() - t0)
     per = sum(times) / len(times)
     value = sample / per
+    single = cpu_sample(tables, ctx, new, kf, vf, seconds=2.0, threads=1)
     out = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-           "config": {"workload": "ragged prefill chunk, Qwen2-7B KV geometry (28 layers, "
-                                  "entry 512); bounded sample per step: 4096 tokens x 28 layers"},
+           "config": {"workload": workload, **extra, "host_threads": arm.threads},
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": arm.threads,
-                            "kind": "port", "sample": arm.describe(len(times))},
+                            "kind": "port", "sample": arm.describe(len(times)) +
+                            f"; each step is this sample on {arm.threads} host threads"},
+           "single_thread": {"value": single["value"], "unit": "tokens/s", "cores": 1,
+                             "sample": single["sample"],
+                             "note": "CpuBackend is single-threaded; the arm's value uses "
+                                     "every host core, a harder baseline"},
            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)

@@ -338,10 +338,19 @@ int pkv_digest_rows_dev(pkv_backend *b, int64_t layer, const void *k, const void
  * followed by pkv_reshape_and_cache_dev.
  *
  * - num_tokens above PKV_NOALLOC_MAX_TOKENS is rejected (ShapeMismatch{max,
- *   num_tokens}) before any device work.
+ *   num_tokens}) before any device work; more than 57,344 sequences is
+ *   rejected as by pkv_resolve_slots_dev (PKV_ERR_DEVICE).
+ * - Pools and sources of f32, bf16 and f16 only: an fp8 (E4M3) pool or
+ *   source is rejected with PKV_ERR_DEVICE, because quantising needs the
+ *   per-(layer, kv head) scales that only a backend holds
+ *   (pkv_resolve_and_cache_dev writes fp8 pools).
+ * - Strides are checked as by pkv_reshape_and_cache_dev: a token stride
+ *   shorter than the entry, or (layer = -1) a layer stride shorter than
+ *   num_tokens x token stride, is ShapeMismatch.
  * - Runs on the current device; the first call on a device looks up the
  *   scratch array's device address, so make that first call before any
- *   stream capture.
+ *   stream capture. The address is kept for the life of the process: calls
+ *   after cudaDeviceReset on that device are not supported.
  * - All calls on a device share the scratch array: calls whose work overlaps
  *   on the GPU race. Each call clears what it needs before use.
  * - device_status (optional, device memory, 2 x int64) receives {status,

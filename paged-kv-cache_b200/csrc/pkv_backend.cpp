@@ -784,9 +784,6 @@ Status B200Backend::zero_blocks_dev(const int64_t *blocks, int64_t count, cudaSt
     return check("zero_blocks", launch_zero(a, st));
 }
 
-// Largest sequence count whose prefix fits in one CTA's shared memory.
-static constexpr int64_t kMaxResolveSeqs = 56 * 1024;
-
 Status B200Backend::resolve_slots_dev(const int32_t *tables, int64_t table_stride,
                                       const int32_t *ctx, const int32_t *new_lens,
                                       int64_t num_seqs, int64_t num_tokens, int32_t *cu,

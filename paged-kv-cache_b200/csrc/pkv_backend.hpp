@@ -8,9 +8,13 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <exception>
 #include <memory>
+#include <new>
 #include <string>
 #include <vector>
+
+#include <nvtx3/nvToolsExt.h>
 
 #include "pkv_b200.h"
 #include "pkv_internal.hpp"
@@ -31,6 +35,27 @@ Status error(int code, int64_t a, int64_t b, std::string msg);
 Status device_error(const std::string &what, cudaError_t e);
 // Stores `s` as this thread's last status (pkv_last_error*) and returns its code.
 int finish(Status s);
+
+// One NVTX range per C-ABI call, named after the entry point.
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+};
+
+// Runs the body of a C-ABI entry point inside its NVTX range and records its
+// status; no exception crosses the boundary (host allocation failures become
+// PKV_ERR_DEVICE).
+template <typename F>
+int guarded(const char *name, F &&f) {
+    NvtxRange range(name);
+    try {
+        return finish(f());
+    } catch (const std::bad_alloc &) {
+        return finish(error(PKV_ERR_DEVICE, 0, 0, "host out of memory"));
+    } catch (const std::exception &e) {
+        return finish(error(PKV_ERR_DEVICE, 0, 0, e.what()));
+    }
+}
 
 class B200Backend {
    public:

@@ -6,10 +6,6 @@
 // tool attached).
 
 #include <cstring>
-#include <exception>
-#include <new>
-
-#include <nvtx3/nvToolsExt.h>
 
 #include "pkv_b200.h"
 #include "pkv_backend.hpp"
@@ -29,6 +25,7 @@ int pkv::finish(pkv::Status s) {
 }
 
 using pkv::finish;
+using pkv::guarded;
 
 namespace {
 
@@ -39,23 +36,6 @@ bool valid_dtype(int t) { return t >= PKV_F32 && t <= PKV_FP8_E4M3; }
 int bad_dtype() { return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "unknown dtype tag")); }
 
 cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
-
-struct NvtxRange {
-    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
-    ~NvtxRange() { nvtxRangePop(); }
-};
-
-template <typename F>
-int guarded(const char *name, F &&f) {
-    NvtxRange range(name);
-    try {
-        return finish(f());
-    } catch (const std::bad_alloc &) {
-        return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "host out of memory"));
-    } catch (const std::exception &e) {
-        return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, e.what()));
-    }
-}
 
 }  // namespace
 

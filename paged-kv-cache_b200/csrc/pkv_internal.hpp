@@ -28,6 +28,10 @@ struct Fp8Scales {
     long long elem_offset = 0;
 };
 
+// Largest sequence count slot resolution takes in one call: the prefix of
+// new_lens is built in one CTA's shared memory.
+constexpr long long kMaxResolveSeqs = 56 * 1024;
+
 // First bad index met by a device entry point. `code` is a pkv_status;
 // `index` is the token / pair / block index it was met at.
 struct DevError {
