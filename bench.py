@@ -526,8 +526,12 @@ def wl_table_batch(run, kind: str) -> dict:
         out["ops"] = {name: {"ms": round(r["ms"], 4), "frac": round(r["frac_of_peak"], 3)}
                       for name, r in ops.items()}
     if not args.no_e2e:
+        pinned = e2e_host_path(args, backend, tables, ctx, new, k, v, run.barrier,
+                               run.max_over_ranks, mode="bf16_pinned")
         out["e2e"] = e2e_host_path(args, backend, tables, ctx, new, k, v, run.barrier,
-                                   run.max_over_ranks)
+                                   run.max_over_ranks, mode="f32_pageable",
+                                   link=pinned["link_h2d_gb_per_s"])
+        out["e2e_bf16_pinned"] = pinned
     if run.rank == 0 and world == 1 and not args.no_cpu:
         n = min(4096, T)
         out["cpu_baseline"] = cpu_sample(tables, ctx, new, k[:, :n].float().cpu().numpy(),
@@ -941,17 +945,51 @@ def wl_trace(run, kind: str) -> dict:
     return out
 
 
-def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks):
-    """Same step through the C ABI's KvBackend entry points with host buffers:
-    per layer pkv_write_kv_batch from pinned bf16 rows (host->device copies in
-    the timed region), then the device error word read back."""
+def link_h2d_gbs(src_np, dev) -> float:
+    """The host link's own ceiling: plain pinned host -> device copies of one
+    layer's K and V rows."""
+    import torch
+
+    src = torch.from_numpy(src_np)
+    if not src.is_pinned():
+        src = src.pin_memory()
+    dst = torch.empty(src.shape, dtype=src.dtype, device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for i in range(4):
+        if i == 1:
+            ev[0].record()
+        dst.copy_(src, non_blocking=True)
+        dst.copy_(src, non_blocking=True)
+    ev[1].record()
+    torch.cuda.synchronize()
+    return 3 * 2 * src.numel() * src.element_size() / (ev[0].elapsed_time(ev[1]) / 1e3) / 1e9
+
+
+def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks,
+                  mode: str = "f32_pageable", link: float | None = None):
+    """Same step through the C ABI's KvBackend entry point with host buffers:
+    per layer pkv_write_kv_batch (host->device copies in the timed region),
+    then the device error word read back.
+
+    mode "f32_pageable": the trait's own call, write_kv_batch(&[f32]) from
+    ordinary (pageable) memory, as a Rust caller holding Vec<f32> rows makes
+    it; the library's host stager narrows the rows to bf16 (round to nearest
+    even) into pinned chunks while earlier chunks upload.
+    mode "bf16_pinned": rows already in bf16 in pinned memory, copied by the
+    DMA engine straight from the caller's buffer."""
     import numpy as np
     import torch
 
     L, T, es = k.shape
     blocks, offs = host_slots(tables, ctx, new, backend.config().block_size)
-    hk = k.view(torch.int16).cpu().pin_memory().numpy().view(np.uint16)
-    hv = v.view(torch.int16).cpu().pin_memory().numpy().view(np.uint16)
+    if mode == "bf16_pinned":
+        hk = k.view(torch.int16).cpu().pin_memory().numpy().view(np.uint16)
+        hv = v.view(torch.int16).cpu().pin_memory().numpy().view(np.uint16)
+        host_dtype, elem = "bf16", 2
+    else:
+        hk = k.float().cpu().numpy()  # pageable: torch's ordinary CPU allocator
+        hv = v.float().cpu().numpy()
+        host_dtype, elem = "f32", 4
     steps = max(1, min(args.steps, 5))
 
     def one():
@@ -959,7 +997,7 @@ def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks
         # (a caller of the trait holds one slice of PhysicalSlots per step).
         pairs = backend.slot_pairs(blocks, offs)
         for layer in range(L):
-            backend.write_kv_batch_pairs(layer, pairs, hk[layer], hv[layer], host_dtype="bf16")
+            backend.write_kv_batch_pairs(layer, pairs, hk[layer], hv[layer], host_dtype=host_dtype)
         if backend.device_error() is not None:
             raise SystemExit("device error in e2e step")
 
@@ -970,26 +1008,25 @@ def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks
         one()
     barrier()
     dt = max_over_ranks(time.perf_counter() - t0)
-    h2d = int(L * (2 * T * es * 2 + T * 8))
-    # The link's own ceiling: plain pinned host -> device copies of one layer's K and V rows.
-    src = torch.from_numpy(hk[0])
-    if not src.is_pinned():
-        src = src.pin_memory()
-    dst = torch.empty(src.shape, dtype=src.dtype, device=k.device)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    for i in range(4):
-        if i == 1:
-            ev[0].record()
-        dst.copy_(src, non_blocking=True)
-        dst.copy_(src, non_blocking=True)
-    ev[1].record()
-    torch.cuda.synchronize()
-    link = 3 * 2 * src.numel() * src.element_size() / (ev[0].elapsed_time(ev[1]) / 1e3) / 1e9
-    step_gbs = h2d * steps / dt / 1e9
-    return {"value": T * steps / dt, "unit": "tokens/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 16, "steps": steps,
-            "h2d_gb_per_s": step_gbs, "link_h2d_gb_per_s": link, "frac_of_link": step_gbs / link,
-            "path": "pkv_write_kv_batch per layer, pinned bf16 host rows, + pkv_device_error"}
+    # Bytes the caller hands over per step (its rows and its destinations).
+    h2d = int(L * (2 * T * es * elem + T * 8))
+    # Bytes that cross the link per step: rows as the pool stores them.
+    moved = int(L * (2 * T * es * 2 + T * 8))
+    if link is None:
+        link = link_h2d_gbs(k[0].view(torch.int16).cpu().numpy(), k.device)
+    moved_gbs = moved * steps / dt / 1e9
+    out = {"value": T * steps / dt, "unit": "tokens/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 16, "steps": steps,
+           "link_bytes_per_step": moved, "link_gb_per_s": moved_gbs,
+           "link_h2d_gb_per_s": link, "frac_of_link": moved_gbs / link}
+    if mode == "bf16_pinned":
+        out["path"] = "pkv_write_kv_batch per layer, pinned bf16 host rows, + pkv_device_error"
+    else:
+        out["path"] = ("pkv_write_kv_batch per layer, PKV_F32 rows in pageable host memory (the "
+                       "trait's write_kv_batch(&[f32])), narrowed to bf16 by the library's host "
+                       "stager, + pkv_device_error")
+        out["host_threads"] = backend.host_threads()
+    return out
 
 
 def bench_ops(backend, cfg, dev, stream, reps: int = 10) -> dict:

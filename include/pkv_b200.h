@@ -366,6 +366,25 @@ int pkv_resolve_and_cache_noalloc(const pkv_config *cfg, int pool_dtype, int sha
                                   int64_t src_token_stride, int64_t src_layer_stride,
                                   int src_dtype, int64_t *device_status, void *stream);
 
+/* Worker threads of the backend's host stager. Large host-buffer writes
+ * (pkv_write_kv_batch / pkv_write_kv of at least 1 MiB of rows) use it when
+ * the rows are in pageable memory, or are f32 rows for a bf16 pool: the
+ * workers copy (or narrow to bf16) the caller's rows into a 64 MiB ring of
+ * pinned chunks while earlier chunks cross the host link, and the call
+ * returns once every row has been read. Environment, read by pkv_create:
+ * PKV_HOST_THREADS=n sets the count (default: one per host core, at most
+ * 16); PKV_HOST_STAGING=off copies from the caller's buffer instead. No
+ * counterpart in the reference (its CudaBackend copies each slice with a
+ * fresh device allocation, crates/paged-kv-cuda/src/backend.rs:177-180). */
+int pkv_host_threads(const pkv_backend *b, int *threads);
+
+/* f32 -> bf16 on the host, round to nearest even (NaN as CUDA's
+ * __float2bfloat16_rn gives it): the narrowing the host stager applies to
+ * f32 rows bound for a bf16 pool before they cross the host link, with the
+ * same results as the device conversion. dst receives bf16 bit patterns.
+ * No counterpart in the reference (its pool is f32). */
+int pkv_f32_to_bf16(const float *src, uint16_t *dst, uint64_t n);
+
 /* Wait for all work issued on the backend's stream. */
 int pkv_sync(pkv_backend *b);
 /* Synchronise, then read and clear the device error word. Returns PKV_OK if no

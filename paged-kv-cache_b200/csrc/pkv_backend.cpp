@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <unordered_map>
@@ -164,6 +165,17 @@ Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int s
         return device_error("cudaGetDeviceProperties", e);
     b->gpu_name_ = prop.name;
     b->sms_ = num_sms(device);
+    // Host staging of large host-buffer writes: PKV_HOST_STAGING=off copies
+    // straight from the caller's buffer instead (as the reference does);
+    // PKV_HOST_THREADS sets the stager's worker count (default: one per
+    // host core, up to 16).
+    if (const char *m = std::getenv("PKV_HOST_STAGING")) b->host_staging_ = std::strcmp(m, "off") != 0;
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    b->host_threads_ = (int)std::min(16u, hw);
+    if (const char *t = std::getenv("PKV_HOST_THREADS")) {
+        const int n = std::atoi(t);
+        if (n > 0) b->host_threads_ = std::min(n, HostStager::kSlots / 2);
+    }
     // A blocking stream: host-buffer calls stay ordered with work that callers
     // issue on the legacy default stream.
     if ((e = cudaStreamCreateWithFlags(&b->stream_, cudaStreamDefault)) != cudaSuccess)
@@ -213,6 +225,7 @@ Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int s
 
 B200Backend::~B200Backend() {
     DeviceGuard g(device_);
+    stager_.reset();  // joins its workers; their copies are on copy_stream_
     if (stream_) cudaStreamSynchronize(stream_);
     if (copy_stream_) cudaStreamSynchronize(copy_stream_);
     if (k_plane_) cudaFree(k_plane_);
@@ -318,6 +331,21 @@ Status B200Backend::ensure_host_stage(size_t bytes) {
     return Status::Ok();
 }
 
+bool B200Backend::host_pinned(const void *p) const {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();  // not a CUDA-known pointer: pageable
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+}
+
+Status B200Backend::stager(HostStager **out) {
+    if (!stager_) stager_.reset(new HostStager(device_, copy_stream_, host_threads_));
+    *out = stager_.get();
+    return Status::Ok();
+}
+
 // ---------------------------------------------------------------------------
 // reshape_and_cache over host buffers
 
@@ -325,7 +353,16 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
                                    const void *k, const void *v, DType host) {
     if (count == 0) return Status::Ok();
     DeviceGuard g(device_);
-    const size_t row_bytes = shard_entry_ * dtype_size(host);
+    // Large batches from pageable memory, and f32 rows for a bf16 pool, go
+    // through the host stager: worker threads copy (or narrow to bf16, which
+    // halves the link bytes) into pinned chunks while earlier chunks upload.
+    // Pinned rows of the pool's own type are copied straight from the caller.
+    const bool narrow = host == DType::F32 && dtype_ == DType::BF16;
+    bool staged = false;
+    if (host_staging_ && count * shard_entry_ * dtype_size(host) >= kStageMinBytes)
+        staged = narrow || !host_pinned(k) || !host_pinned(v);
+    const DType sd = staged && narrow ? DType::BF16 : host;  // type of the rows on the device
+    const size_t row_bytes = shard_entry_ * dtype_size(sd);
     const size_t slot_bytes = round_up(count * sizeof(int64_t), kAlign);
     const size_t kv_bytes = round_up(count * row_bytes, kAlign);
     const int buf = scatter_turn_;
@@ -349,16 +386,28 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
     // the other staging buffer) still runs. Rows past a failing destination
     // are copied too but never scattered.
     cudaError_t e;
-    if ((e = cudaStreamWaitEvent(copy_stream_, scatter_free_[buf], 0)) ||
-        (e = cudaMemcpyAsync(d_k, k, count * row_bytes, cudaMemcpyHostToDevice, copy_stream_)) ||
-        (e = cudaMemcpyAsync(d_v, v, count * row_bytes, cudaMemcpyHostToDevice, copy_stream_)) ||
-        (e = cudaEventRecord(inputs_consumed_, copy_stream_))) {
+    if (staged) {
+        HostStager *hs = nullptr;
+        Status st = stager(&hs);
+        if (!st.ok()) return st;
+        const uint64_t n = count * shard_entry_;
+        if ((e = cudaStreamWaitEvent(copy_stream_, scatter_free_[buf], 0)) ||
+            (e = hs->begin(k, host, d_k, sd, n)) || (e = hs->begin(v, host, d_v, sd, n))) {
+            hs->wait();  // never return while a worker may still read the caller's rows
+            return device_error("staging K/V", e);
+        }
+    } else if ((e = cudaStreamWaitEvent(copy_stream_, scatter_free_[buf], 0)) ||
+               (e = cudaMemcpyAsync(d_k, k, count * row_bytes, cudaMemcpyHostToDevice, copy_stream_)) ||
+               (e = cudaMemcpyAsync(d_v, v, count * row_bytes, cudaMemcpyHostToDevice, copy_stream_)) ||
+               (e = cudaEventRecord(inputs_consumed_, copy_stream_))) {
         cudaStreamSynchronize(copy_stream_);  // never return while a copy may still read the caller's rows
         return device_error("staging K/V", e);
     }
-    // The caller's slices are borrowed: return only once they have been read.
+    // The caller's slices are borrowed: return only once they have been read
+    // (by the copy engine, or by the stager's workers, whose pinned chunks
+    // may still be uploading when this call returns).
     auto finish_with = [&](Status st) {
-        const cudaError_t w = cudaEventSynchronize(inputs_consumed_);
+        const cudaError_t w = staged ? stager_->wait() : cudaEventSynchronize(inputs_consumed_);
         if (st.ok() && w != cudaSuccess) return device_error("staging K/V", w);
         return st;
     };
@@ -390,6 +439,11 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
         for (uint64_t i = 0; i < valid; ++i)
             if (hs[i] >= 0) seen_[(uint64_t)hs[i] >> 6] = 0;
     }
+    if (staged) {
+        // Every chunk's copy is issued once wait() returns.
+        if ((e = stager_->wait()) || (e = cudaEventRecord(inputs_consumed_, copy_stream_)))
+            return finish_with(device_error("staging K/V", e));
+    }
     if ((e = cudaMemcpyAsync(d_slots, hs, valid * sizeof(int64_t), cudaMemcpyHostToDevice, stream_)) ||
         (e = cudaEventRecord(h_stage_free_, stream_)) ||
         (e = cudaStreamWaitEvent(stream_, inputs_consumed_, 0)))
@@ -408,7 +462,7 @@ Status B200Backend::launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_
     a.entry_elems = (long long)shard_entry_;
     a.slots = reinterpret_cast<const long long *>(d_slots);
     a.num_tokens = (long long)valid;
-    a.src_dtype = host;
+    a.src_dtype = sd;
     a.pool_dtype = dtype_;
     a.err = d_err_;
     a.fp8 = fp8_scales();

@@ -18,6 +18,7 @@
 
 #include "pkv_b200.h"
 #include "pkv_internal.hpp"
+#include "pkv_stage.hpp"
 
 namespace pkv {
 
@@ -119,6 +120,7 @@ class B200Backend {
     uint64_t full_entry_elems() const { return cfg_.num_kv_heads * cfg_.head_dim; }
     uint64_t elem_offset() const { return shard_rank_ * shard_entry_; }
     int shard_rank() const { return shard_rank_; }
+    int host_threads() const { return host_threads_; }
     int num_shards() const { return num_shards_; }
     void *k_plane() const { return k_plane_; }
     void *v_plane() const { return v_plane_; }
@@ -138,6 +140,8 @@ class B200Backend {
     Status ensure_host_stage(size_t bytes);
     Status launch_scatter(uint64_t layer, const pkv_slot *dsts, uint64_t count, const void *k,
                           const void *v, DType host);
+    bool host_pinned(const void *p) const;
+    Status stager(HostStager **out);
     Status launch_copy_pairs(const uint64_t *pairs, uint64_t count);
     Status launch_zero_ids(const uint64_t *blocks, uint64_t count);
     cudaError_t launch_copy(const CopyLaunch &a, cudaStream_t st) const;
@@ -177,6 +181,11 @@ class B200Backend {
     cudaEvent_t scatter_free_[2] = {nullptr, nullptr};
     int scatter_turn_ = 0;
     std::vector<uint64_t> seen_;  // one bit per slot of a layer: duplicate detection
+    // Host stager for large host-buffer writes (made on first use).
+    static constexpr uint64_t kStageMinBytes = 1u << 20;
+    std::unique_ptr<HostStager> stager_;
+    bool host_staging_ = true;
+    int host_threads_ = 16;
     // fp8 pools: [num_layers][num_kv_heads] scales on the host, and their f32
     // reciprocals on the device (K's, then V's).
     std::vector<float> k_scale_, v_scale_;

@@ -286,6 +286,20 @@ int pkv_digest_rows_dev(pkv_backend *b, int64_t layer, const void *k, const void
     });
 }
 
+int pkv_host_threads(const pkv_backend *b, int *threads) {
+    if (!b || !threads) return null_handle();
+    *threads = b->impl->host_threads();
+    return finish(pkv::Status::Ok());
+}
+
+int pkv_f32_to_bf16(const float *src, uint16_t *dst, uint64_t n) {
+    if (n > 0 && (!src || !dst)) return finish(pkv::error(PKV_ERR_DEVICE, 0, 0, "null argument"));
+    return guarded("pkv_f32_to_bf16", [&] {
+        pkv::narrow_f32_to_bf16(dst, src, n);
+        return pkv::Status::Ok();
+    });
+}
+
 int pkv_sync(pkv_backend *b) {
     if (!b) return null_handle();
     return guarded("pkv_sync", [&] { return b->impl->sync(); });

@@ -81,6 +81,8 @@ _PROTOS = {
                                            _I64, _I64, _P, _I64, _P, _P, _I64, _I64, _I, _P, _P]),
     "pkv_digest_rows_dev": (_I, [_P, _I64, _P, _P, _I64, _I64, _P, _I64, _I, C.POINTER(_U64),
                                  C.POINTER(_U64), _P]),
+    "pkv_f32_to_bf16": (_I, [_P, _P, _U64]),
+    "pkv_host_threads": (_I, [_P, C.POINTER(_I)]),
     "pkv_sync": (_I, [_P]),
     "pkv_device_error": (_I, [_P, C.POINTER(_I64)]),
 }

@@ -164,6 +164,12 @@ class B200Backend:
         """write_kv_batch with the destinations given as two integer arrays."""
         self.write_kv_batch_pairs(layer, self.slot_pairs(blocks, slots), k, v, host_dtype)
 
+    def host_threads(self) -> int:
+        """Worker threads of the library's host stager (PKV_HOST_THREADS)."""
+        n = C.c_int()
+        _check(lib.pkv_host_threads(self._h, C.byref(n)))
+        return n.value
+
     def read_kv(self, layer: int, src, k_out: np.ndarray, v_out: np.ndarray) -> None:
         """backend.rs:82-88: fills k_out and v_out (f32, f16, or uint16 = bf16 bits)."""
         tag = _host_array(k_out[:0], None)[1]
