@@ -526,12 +526,11 @@ def wl_table_batch(run, kind: str) -> dict:
         out["ops"] = {name: {"ms": round(r["ms"], 4), "frac": round(r["frac_of_peak"], 3)}
                       for name, r in ops.items()}
     if not args.no_e2e:
-        pinned = e2e_host_path(args, backend, tables, ctx, new, k, v, run.barrier,
-                               run.max_over_ranks, mode="bf16_pinned")
         out["e2e"] = e2e_host_path(args, backend, tables, ctx, new, k, v, run.barrier,
-                                   run.max_over_ranks, mode="f32_pageable",
-                                   link=pinned["link_h2d_gb_per_s"])
-        out["e2e_bf16_pinned"] = pinned
+                                   run.max_over_ranks, mode="bf16_pinned")
+        out["e2e_f32"] = e2e_host_path(args, backend, tables, ctx, new, k, v, run.barrier,
+                                       run.max_over_ranks, mode="f32_pageable",
+                                       link=out["e2e"]["link_h2d_gb_per_s"])
     if run.rank == 0 and world == 1 and not args.no_cpu:
         n = min(4096, T)
         out["cpu_baseline"] = cpu_sample(tables, ctx, new, k[:, :n].float().cpu().numpy(),
@@ -954,15 +953,17 @@ def link_h2d_gbs(src_np, dev) -> float:
     if not src.is_pinned():
         src = src.pin_memory()
     dst = torch.empty(src.shape, dtype=src.dtype, device=dev)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    for i in range(4):
-        if i == 1:
-            ev[0].record()
-        dst.copy_(src, non_blocking=True)
-        dst.copy_(src, non_blocking=True)
-    ev[1].record()
-    torch.cuda.synchronize()
-    return 3 * 2 * src.numel() * src.element_size() / (ev[0].elapsed_time(ev[1]) / 1e3) / 1e9
+    best = 0.0
+    dst.copy_(src, non_blocking=True)
+    for _ in range(5):  # best of 5 runs of 4 back-to-back copies
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record()
+        for _ in range(4):
+            dst.copy_(src, non_blocking=True)
+        ev[1].record()
+        torch.cuda.synchronize()
+        best = max(best, 4 * src.numel() * src.element_size() / (ev[0].elapsed_time(ev[1]) / 1e3) / 1e9)
+    return best
 
 
 def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks,

@@ -174,7 +174,16 @@ Status B200Backend::create(const pkv_config &cfg, DType dtype, int device, int s
     b->host_threads_ = (int)std::min(16u, hw);
     if (const char *t = std::getenv("PKV_HOST_THREADS")) {
         const int n = std::atoi(t);
-        if (n > 0) b->host_threads_ = std::min(n, HostStager::kSlots / 2);
+        if (n > 0) b->host_threads_ = std::min(n, HostStager::kMaxSlots / 2);
+    }
+    // Ring geometry (tuning): PKV_STAGE_CHUNK_KIB per chunk, PKV_STAGE_SLOTS chunks.
+    if (const char *c = std::getenv("PKV_STAGE_CHUNK_KIB")) {
+        const long n = std::atol(c);
+        if (n > 0) b->stage_chunk_bytes_ = size_t(n) << 10;
+    }
+    if (const char *c = std::getenv("PKV_STAGE_SLOTS")) {
+        const int n = std::atoi(c);
+        if (n > 0) b->stage_slots_ = n;
     }
     // A blocking stream: host-buffer calls stay ordered with work that callers
     // issue on the legacy default stream.
@@ -341,7 +350,9 @@ bool B200Backend::host_pinned(const void *p) const {
 }
 
 Status B200Backend::stager(HostStager **out) {
-    if (!stager_) stager_.reset(new HostStager(device_, copy_stream_, host_threads_));
+    if (!stager_)
+        stager_.reset(new HostStager(device_, copy_stream_, host_threads_, stage_chunk_bytes_,
+                                     stage_slots_));
     *out = stager_.get();
     return Status::Ok();
 }

@@ -7,6 +7,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <exception>
 #include <memory>
@@ -120,7 +121,10 @@ class B200Backend {
     uint64_t full_entry_elems() const { return cfg_.num_kv_heads * cfg_.head_dim; }
     uint64_t elem_offset() const { return shard_rank_ * shard_entry_; }
     int shard_rank() const { return shard_rank_; }
-    int host_threads() const { return host_threads_; }
+    // Workers the stager runs with (it caps them at half its ring's slots).
+    int host_threads() const {
+        return std::max(1, std::min(host_threads_, std::min(stage_slots_, HostStager::kMaxSlots) / 2));
+    }
     int num_shards() const { return num_shards_; }
     void *k_plane() const { return k_plane_; }
     void *v_plane() const { return v_plane_; }
@@ -186,6 +190,8 @@ class B200Backend {
     std::unique_ptr<HostStager> stager_;
     bool host_staging_ = true;
     int host_threads_ = 16;
+    size_t stage_chunk_bytes_ = 1u << 20;
+    int stage_slots_ = 32;
     // fp8 pools: [num_layers][num_kv_heads] scales on the host, and their f32
     // reciprocals on the device (K's, then V's).
     std::vector<float> k_scale_, v_scale_;

@@ -41,10 +41,16 @@ void narrow_f32_to_bf16(uint16_t *dst, const float *src, uint64_t n) {
         }
 }
 
-HostStager::HostStager(int device, cudaStream_t upload_stream, int threads)
-    : device_(device), stream_(upload_stream) {
-    for (int s = 0; s < kSlots; ++s) issued_[s] = -1;
-    threads = std::max(1, std::min(threads, kSlots / 2));
+HostStager::HostStager(int device, cudaStream_t upload_stream, int threads, size_t chunk_bytes,
+                       int slots)
+    : device_(device),
+      stream_(upload_stream),
+      chunk_bytes_(std::max<size_t>(4096, chunk_bytes / 4096 * 4096)),
+      slots_(std::max(2, std::min(slots, kMaxSlots))) {
+    for (int s = 0; s < kMaxSlots; ++s) issued_[s] = -1;
+    // Each worker holds at most one slot, and a slot waits only on the chunk
+    // taken slots_ chunks before it: up to slots_ / 2 workers stream.
+    threads = std::max(1, std::min(threads, slots_ / 2));
     for (int i = 0; i < threads; ++i) workers_.emplace_back([this] { run(); });
 }
 
@@ -74,7 +80,7 @@ cudaError_t HostStager::ensure_ring() {
     for (auto &ev : slot_free_)
         if (!ev && (e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess) return e;
     void *p = nullptr;
-    if ((e = cudaMallocHost(&p, size_t(kSlots) * kChunkBytes)) != cudaSuccess) return e;
+    if ((e = cudaMallocHost(&p, size_t(slots_) * chunk_bytes_)) != cudaSuccess) return e;
     ring_ = static_cast<char *>(p);
     return cudaSuccess;
 }
@@ -85,7 +91,7 @@ cudaError_t HostStager::begin(const void *src, DType in, void *dst, DType out, u
     const cudaError_t e = ensure_ring();
     if (e != cudaSuccess) return e;
     const uint64_t in_size = dtype_size(in), out_size = dtype_size(out);
-    const uint64_t per = kChunkBytes / out_size;
+    const uint64_t per = chunk_bytes_ / out_size;
     {
         std::lock_guard<std::mutex> lk(mu_);
         for (uint64_t off = 0; off < elems; off += per) {
@@ -118,12 +124,12 @@ void HostStager::run() {
             if (jobs_.empty()) return;  // stopping
             j = jobs_.front();
             jobs_.pop_front();
-            s = int(j.seq % kSlots);
+            s = int(j.seq % slots_);
             // The slot's previous chunk was taken before this one; wait until
             // its copy has been issued, so that the slot's event covers it.
-            cv_done_.wait(lk, [&] { return issued_[s] >= j.seq - kSlots; });
+            cv_done_.wait(lk, [&] { return issued_[s] >= j.seq - slots_; });
         }
-        char *buf = ring_ + size_t(s) * kChunkBytes;
+        char *buf = ring_ + size_t(s) * chunk_bytes_;
         cudaError_t e = cudaEventSynchronize(slot_free_[s]);  // its copy has left the slot
         if (e == cudaSuccess) {
             if (j.in == j.out)

@@ -30,7 +30,9 @@ void narrow_f32_to_bf16(uint16_t *dst, const float *src, uint64_t n);
 
 class HostStager {
    public:
-    HostStager(int device, cudaStream_t upload_stream, int threads);
+    // `chunk_bytes` (a multiple of 4 KiB) and `slots` size the pinned ring.
+    HostStager(int device, cudaStream_t upload_stream, int threads, size_t chunk_bytes,
+               int slots);
     ~HostStager();
     HostStager(const HostStager &) = delete;
     HostStager &operator=(const HostStager &) = delete;
@@ -44,8 +46,7 @@ class HostStager {
 
     int threads() const { return (int)workers_.size(); }
 
-    static constexpr size_t kChunkBytes = 2u << 20;  // staged bytes per chunk
-    static constexpr int kSlots = 32;                 // ring of 64 MiB pinned
+    static constexpr int kMaxSlots = 64;
 
    private:
     struct Job {
@@ -53,20 +54,22 @@ class HostStager {
         char *dst;
         uint64_t elems;
         DType in, out;
-        int64_t seq;  // global chunk number; slot = seq % kSlots
+        int64_t seq;  // global chunk number; slot = seq % slots_
     };
     void run();
     cudaError_t ensure_ring();
 
     int device_;
     cudaStream_t stream_;
-    char *ring_ = nullptr;  // kSlots x kChunkBytes, pinned
-    cudaEvent_t slot_free_[kSlots] = {};
+    size_t chunk_bytes_;    // staged bytes per chunk
+    int slots_;
+    char *ring_ = nullptr;  // slots_ x chunk_bytes_, pinned
+    cudaEvent_t slot_free_[kMaxSlots] = {};
     std::vector<std::thread> workers_;
     std::mutex mu_;
     std::condition_variable cv_jobs_, cv_done_;
     std::deque<Job> jobs_;
-    int64_t issued_[kSlots];  // last chunk whose copy left slot i (issued)
+    int64_t issued_[kMaxSlots];  // last chunk whose copy left slot i (issued)
     int64_t next_seq_ = 0;
     int64_t queued_ = 0, done_ = 0;
     cudaError_t err_ = cudaSuccess;
