@@ -936,6 +936,12 @@ def wl_trace(run, kind: str) -> dict:
                         "rejected": st[-1]["rejected"],
                         "running_final": st[-1]["running"],
                         "utilization_max": max(s["utilization"] for s in st)}
+    out["verify"] = last_step_landed(run, backend, timed[-1], k, v)
+    if not out["verify"]["ok"]:
+        raise SystemExit(f"bench: trace verification failed: {out['verify']}")
+    if world > 1:
+        out["ranks"] = rank_breakdown(run, stepper.step_ms(), write_bytes,
+                                      ph["resolve_and_cache"] + ph["reshape_and_cache"])
     out["host_driver_s"] = host_s
     out["gpu_launches"] = stepper.launches
     out["clocks"] = {**clocks.summary(),
@@ -964,6 +970,62 @@ def link_h2d_gbs(src_np, dev) -> float:
         torch.cuda.synchronize()
         best = max(best, 4 * src.numel() * src.element_size() / (ev[0].elapsed_time(ev[1]) / 1e3) / 1e9)
     return best
+
+
+def last_step_landed(run, backend, plan, k, v) -> dict:
+    """After a trace: every token the last step wrote from a host-known slot
+    (nothing later overwrote them) holds its row, in 3 layers of this rank's
+    shard; the per-rank results are all-gathered (NCCL) and must all hold."""
+    import numpy as np
+
+    torch = run.torch
+    L, R, es = k.shape
+    tr = plan.resolved_tokens
+    slots = np.asarray(plan.direct_slots, np.int64)
+    ok = True
+    if len(slots):
+        d_slots = torch.from_numpy(slots).to(run.dev)
+        rows = torch.from_numpy((tr + np.arange(len(slots))) % R).to(run.dev)
+        pk, pv = backend.planes()
+        for l in (0, L // 2, L - 1):
+            ok &= bool(torch.equal(pk[l].reshape(-1, es)[d_slots], k[l, rows]))
+            ok &= bool(torch.equal(pv[l].reshape(-1, es)[d_slots], v[l, rows]))
+    flag = torch.tensor([1 if ok else 0, len(slots)], dtype=torch.int64, device=run.dev)
+    if run.world > 1:
+        got = [torch.empty_like(flag) for _ in range(run.world)]
+        run.dist.all_gather(got, flag)
+    else:
+        got = [flag]
+    per = [bool(g[0].item()) for g in got]
+    return {"ok": all(per), "ranks_ok": per, "tokens_checked_per_rank": int(len(slots)),
+            "check": "last step's host-slot tokens hold their rows in layers 0, L/2, L-1 of "
+                     "every shard" + (" (all_gather over NCCL)" if run.world > 1 else "")}
+
+
+def rank_breakdown(run, step_ms: list[float], write_bytes: float, write_ms: float) -> dict:
+    """Per-rank view of a multi-GPU trace: each rank's device time over the
+    timed steps, how many steps each rank bounds (is the slowest on), and
+    each rank's token-write bandwidth as a fraction of the measured peak.
+    All ranks call the same collectives in the same order."""
+    torch, dist = run.torch, run.dist
+    t = torch.tensor(step_ms, dtype=torch.float64, device=run.dev)
+    per = [torch.empty_like(t) for _ in range(run.world)]
+    dist.all_gather(per, t)
+    m = torch.stack(per)  # [rank][step]
+    w = torch.tensor([write_ms], dtype=torch.float64, device=run.dev)
+    ws = [torch.empty_like(w) for _ in range(run.world)]
+    dist.all_gather(ws, w)
+    peak, _ = measured_peak_gbs()
+    bounds = torch.bincount(m.argmax(0), minlength=run.world).tolist()
+    return {
+        "device_ms_per_rank": [round(x, 3) for x in m.sum(1).tolist()],
+        "steps_bounded_by_rank": bounds,
+        "token_write_frac_of_peak_per_rank": [
+            round(write_bytes / (float(x.item()) / 1e3) / 1e9 / peak, 4) if float(x.item()) else None
+            for x in ws],
+        "note": "a step's device time is its first to last phase mark on that rank; the rank "
+                "with the longest time bounds the step",
+    }
 
 
 def e2e_host_path(args, backend, tables, ctx, new, k, v, barrier, max_over_ranks,

@@ -175,6 +175,11 @@ class DeviceStepper:
             out["total"] = self.events[0][0].elapsed_time(self.events[-1][-1])
         return out
 
+    def step_ms(self) -> list[float]:
+        """Device milliseconds of each recorded step (first to last phase mark)."""
+        self.stream.synchronize()
+        return [m[0].elapsed_time(m[-1]) for m in self.events]
+
     def reset_timing(self) -> None:
         self.events = []
 
@@ -273,27 +278,3 @@ class Prepared:
         self.t, self.s = self.tr + self.d, len(plan.new)
         self.table_shape, self.table_elems = tables.shape, tables.size
         self.nzero = len(plan.zero)
-
-
-def apply_to_oracle(orc, plan: StepPlan, k: np.ndarray, v: np.ndarray, resolve) -> None:
-    """The same step on the CPU oracle (CpuBackend semantics): copies, writes
-    of every token (slots resolved by the oracle's slot rule), zeroes.
-    k, v: f32 [L][R][entry]; token i uses row i % R."""
-    cfg = orc.cfg
-    bs = cfg.block_size
-    if len(plan.copies):
-        orc.copy_blocks(plan.copies)
-    tr = plan.resolved_tokens
-    if len(plan.new):
-        rc, _, res = resolve(plan.tables, plan.ctx, plan.new, tr, bs, cfg.num_blocks)
-        assert rc == 0
-    else:
-        res = np.zeros(0, np.int64)
-    slots = np.concatenate([res, plan.direct_slots.astype(np.int64)])
-    rows = np.arange(len(slots)) % k.shape[1]
-    keep = slots >= 0
-    dsts = [(int(x) // bs, int(x) % bs) for x in slots[keep]]
-    for layer in range(cfg.num_layers):
-        orc.write_kv_batch(layer, dsts, k[layer][rows[keep]].ravel(), v[layer][rows[keep]].ravel())
-    if len(plan.zero):
-        orc.zero_blocks(plan.zero)

@@ -10,11 +10,35 @@ import pytest
 
 from oracle.cpu import OracleBackend, resolve_slots
 from pagedkv import B200Backend, CacheConfig
-from pagedkv.driver import DeviceStepper, apply_to_oracle
-from pagedkv.traces import beam_cow_trace, churn_trace, plan_from_batch
+from pagedkv.driver import DeviceStepper
+from pagedkv.traces import StepPlan, beam_cow_trace, churn_trace, plan_from_batch
 from pagedkv.workloads import Stream, bf16_bits_to_f32, decode_batch, f32_to_bf16_bits, prefill_chunk
 
 pytestmark = pytest.mark.gpu
+
+
+def apply_to_oracle(orc, plan: StepPlan, k: np.ndarray, v: np.ndarray, resolve) -> None:
+    """The same step on the CPU oracle (CpuBackend semantics): copies, writes
+    of every token (slots resolved by the oracle's slot rule), zeroes.
+    k, v: f32 [L][R][entry]; token i uses row i % R."""
+    cfg = orc.cfg
+    bs = cfg.block_size
+    if len(plan.copies):
+        orc.copy_blocks(plan.copies)
+    tr = plan.resolved_tokens
+    if len(plan.new):
+        rc, _, res = resolve(plan.tables, plan.ctx, plan.new, tr, bs, cfg.num_blocks)
+        assert rc == 0
+    else:
+        res = np.zeros(0, np.int64)
+    slots = np.concatenate([res, plan.direct_slots.astype(np.int64)])
+    rows = np.arange(len(slots)) % k.shape[1]
+    keep = slots >= 0
+    dsts = [(int(x) // bs, int(x) % bs) for x in slots[keep]]
+    for layer in range(cfg.num_layers):
+        orc.write_kv_batch(layer, dsts, k[layer][rows[keep]].ravel(), v[layer][rows[keep]].ravel())
+    if len(plan.zero):
+        orc.zero_blocks(plan.zero)
 
 
 def rows(cfg, r, seed):
