@@ -5,8 +5,9 @@
 // contiguous moves. Here one thread per CTA hands them to the SM's bulk-copy
 // engine: cp.async.bulk global -> shared (completing on an mbarrier), then
 // cp.async.bulk shared -> global, through a ring of kStages shared-memory
-// buffers so that loads of later chunks overlap stores of earlier ones. No
-// multicast, no tensor map: plain 1-D bulk copies of 16-byte-aligned runs.
+// buffers so that loads of later chunks overlap stores of earlier ones. Each
+// CTA reads only for itself, with no tensor map: plain 1-D bulk copies of
+// 16-byte-aligned runs.
 //
 // Same work and results as copy_blocks_kernel (pkv_kernels.cu); pairs with an
 // id outside the pool are skipped and recorded, self-copies are skipped. Every
