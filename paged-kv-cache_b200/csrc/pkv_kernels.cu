@@ -246,6 +246,90 @@ zero_blocks_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_
     }
 }
 
+// ---- copy_blocks / zero_blocks over small block planes ---------------------
+//
+// A head-sharded pool has small block planes (2 KiB per plane and layer at
+// 8 shards of Qwen2-7B's 512-element entry). One CTA per plane would move a
+// few hundred bytes; instead `group` consecutive units (unit u = (pair or
+// block index, layer, plane), u = (index * L + layer) * 2 + plane) share a
+// CTA of kThreads * UNROLL vectors, consecutive threads on consecutive
+// vectors of a unit. `shift` is log2(nvec) when nvec is a power of two.
+
+struct UnitGroups {
+    int nvec;   // vectors per unit (a block plane)
+    int group;  // units per CTA
+    int shift;  // log2(nvec) or -1
+    int num_layers;
+    unsigned num_units;  // < 2^31 (checked by the launcher)
+};
+
+// Unit, vector, index (pair or block id slot), layer and plane of this
+// thread's u-th vector; false past the group or the last unit.
+__device__ __forceinline__ bool group_unit(const UnitGroups &m, int u, int &vec, unsigned &idx,
+                                           int &layer, int &plane) {
+    const int local = u * kThreads + (int)threadIdx.x;
+    const int du = m.shift >= 0 ? local >> m.shift : local / m.nvec;
+    if (du >= m.group) return false;
+    vec = local - du * m.nvec;
+    const unsigned unit = blockIdx.x * (unsigned)m.group + (unsigned)du;
+    if (unit >= m.num_units) return false;
+    plane = (int)(unit & 1u);
+    const unsigned lp = unit >> 1;
+    idx = lp / (unsigned)m.num_layers;
+    layer = (int)(lp - idx * (unsigned)m.num_layers);
+    return true;
+}
+
+template <typename V, int UNROLL>
+__global__ void __launch_bounds__(kThreads)
+copy_blocks_grouped_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_layer,
+                           long long block_bytes, const long long *__restrict__ pairs,
+                           long long num_blocks, UnitGroups m, DevError *err) {
+    V r[UNROLL];
+    V *dst_at[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+        dst_at[u] = nullptr;
+        int vec, layer, plane;
+        unsigned pair;
+        if (!group_unit(m, u, vec, pair, layer, plane)) continue;
+        const long long src = __ldg(pairs + 2 * (long long)pair);
+        const long long dst = __ldg(pairs + 2 * (long long)pair + 1);
+        if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {
+            if (vec == 0 && plane == 0 && layer == 0) record_error(err, kInvalidBlock, pair);
+            continue;
+        }
+        if (src == dst) continue;
+        char *base = (plane ? vp : kp) + layer * pool_layer;
+        r[u] = __ldcs(reinterpret_cast<const V *>(base + src * block_bytes) + vec);
+        dst_at[u] = reinterpret_cast<V *>(base + dst * block_bytes) + vec;
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+        if (dst_at[u]) __stcs(dst_at[u], r[u]);
+}
+
+template <typename V, int UNROLL>
+__global__ void __launch_bounds__(kThreads)
+zero_blocks_grouped_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_layer,
+                           long long block_bytes, const long long *__restrict__ ids,
+                           long long num_blocks, UnitGroups m, DevError *err) {
+    V z;
+    memset(&z, 0, sizeof(V));
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+        int vec, layer, plane;
+        unsigned idx;
+        if (!group_unit(m, u, vec, idx, layer, plane)) continue;
+        const long long blk = __ldg(ids + idx);
+        if (blk < 0 || blk >= num_blocks) {
+            if (vec == 0 && plane == 0 && layer == 0) record_error(err, kInvalidBlock, idx);
+            continue;
+        }
+        __stcs(reinterpret_cast<V *>((plane ? vp : kp) + layer * pool_layer + blk * block_bytes) + vec, z);
+    }
+}
+
 // ---- slot resolution -----------------------------------------------------------
 //
 // Every CTA scans new_lens into shared memory (exclusive prefix, one
@@ -682,12 +766,36 @@ cudaError_t launch_reshape(const ReshapeLaunch &a, int sms, cudaStream_t st) {
 }
 
 namespace {
+// Small block planes (at most half of a CTA's kThreads * U vectors) go to
+// the grouped kernels; larger ones take one CTA per (unit, chunk).
+template <typename V, int U>
+bool small_planes(long long block_bytes, long long num_layers, long long units, UnitGroups &m,
+                  long long &grid) {
+    const long long nvec = block_bytes / (long long)sizeof(V);
+    if (nvec * 2 > kThreads * U || units >= (1ll << 31)) return false;
+    m.nvec = (int)nvec;
+    m.group = (int)(kThreads * U / nvec);
+    m.shift = (nvec & (nvec - 1)) == 0 ? __builtin_ctzll((unsigned long long)nvec) : -1;
+    m.num_layers = (int)num_layers;
+    m.num_units = (unsigned)units;
+    grid = (units + m.group - 1) / m.group;
+    return true;
+}
+
 template <typename V>
 cudaError_t copy_v(const CopyLaunch &a, cudaStream_t st) {
     constexpr int U = 4;
+    UnitGroups m;
+    long long grid;
+    if (small_planes<V, U>(a.block_bytes, a.num_layers, a.num_pairs * a.num_layers * 2, m, grid)) {
+        copy_blocks_grouped_kernel<V, U><<<(unsigned)grid, kThreads, 0, st>>>(
+            static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool),
+            a.num_blocks * a.block_bytes, a.block_bytes, a.pairs, a.num_blocks, m, a.err);
+        return cudaGetLastError();
+    }
     const long long nvec = a.block_bytes / (long long)sizeof(V);
     const int chunks = (int)((nvec + kThreads * U - 1) / (kThreads * U));
-    const long long grid = a.num_pairs * a.num_layers * 2 * chunks;
+    grid = a.num_pairs * a.num_layers * 2 * chunks;
     copy_blocks_kernel<V, U><<<(unsigned)grid, kThreads, 0, st>>>(
         static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool),
         a.num_blocks * a.block_bytes, a.block_bytes, a.pairs, a.num_blocks, (int)a.num_layers,
@@ -697,9 +805,17 @@ cudaError_t copy_v(const CopyLaunch &a, cudaStream_t st) {
 template <typename V>
 cudaError_t zero_v(const ZeroLaunch &a, cudaStream_t st) {
     constexpr int U = 4;
+    UnitGroups m;
+    long long grid;
+    if (small_planes<V, U>(a.block_bytes, a.num_layers, a.num_ids * a.num_layers * 2, m, grid)) {
+        zero_blocks_grouped_kernel<V, U><<<(unsigned)grid, kThreads, 0, st>>>(
+            static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool),
+            a.num_blocks * a.block_bytes, a.block_bytes, a.blocks, a.num_blocks, m, a.err);
+        return cudaGetLastError();
+    }
     const long long nvec = a.block_bytes / (long long)sizeof(V);
     const int chunks = (int)((nvec + kThreads * U - 1) / (kThreads * U));
-    const long long grid = a.num_ids * a.num_layers * 2 * chunks;
+    grid = a.num_ids * a.num_layers * 2 * chunks;
     zero_blocks_kernel<V, U><<<(unsigned)grid, kThreads, 0, st>>>(
         static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool),
         a.num_blocks * a.block_bytes, a.block_bytes, a.blocks, a.num_blocks, (int)a.num_layers,
