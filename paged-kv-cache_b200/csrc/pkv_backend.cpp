@@ -849,6 +849,32 @@ Status B200Backend::zero_blocks_dev(const int64_t *blocks, int64_t count, cudaSt
     return check("zero_blocks", launch_zero(a, st));
 }
 
+Status B200Backend::copy_zero_dev(const int64_t *srcs, const int64_t *dst_off, const int64_t *dsts,
+                                  const int64_t *zero_src, int64_t num_srcs,
+                                  const int64_t *zero_ids, int64_t num_zero, cudaStream_t st) {
+    if (num_srcs < 0 || num_zero < 0)
+        return error(PKV_ERR_SHAPE_MISMATCH, 0, std::min(num_srcs, num_zero), "negative count");
+    if (num_srcs == 0 && num_zero == 0) return Status::Ok();
+    if ((num_srcs > 0 && (!srcs || !dst_off || !dsts || !zero_src)) || (num_zero > 0 && !zero_ids))
+        return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    DeviceGuard g(device_);
+    CopyZeroLaunch a{};
+    a.k_pool = k_plane_;
+    a.v_pool = v_plane_;
+    a.num_layers = (long long)cfg_.num_layers;
+    a.num_blocks = (long long)cfg_.num_blocks;
+    a.block_bytes = (long long)block_bytes();
+    a.srcs = reinterpret_cast<const long long *>(srcs);
+    a.dst_off = reinterpret_cast<const long long *>(dst_off);
+    a.dsts = reinterpret_cast<const long long *>(dsts);
+    a.zero_src = reinterpret_cast<const long long *>(zero_src);
+    a.num_srcs = num_srcs;
+    a.zero_ids = reinterpret_cast<const long long *>(zero_ids);
+    a.num_zero = num_zero;
+    a.err = d_err_;
+    return check("copy_zero_blocks", launch_copy_zero(a, st));
+}
+
 Status B200Backend::resolve_slots_dev(const int32_t *tables, int64_t table_stride,
                                       const int32_t *ctx, const int32_t *new_lens,
                                       int64_t num_seqs, int64_t num_tokens, int32_t *cu,

@@ -88,6 +88,9 @@ class B200Backend {
                                  DType src, cudaStream_t s);
     Status copy_blocks_dev(const int64_t *pairs, int64_t count, cudaStream_t s);
     Status zero_blocks_dev(const int64_t *blocks, int64_t count, cudaStream_t s);
+    Status copy_zero_dev(const int64_t *srcs, const int64_t *dst_off, const int64_t *dsts,
+                         const int64_t *zero_src, int64_t num_srcs, const int64_t *zero_ids,
+                         int64_t num_zero, cudaStream_t s);
     Status set_copy_engine(int engine);
     Status set_kv_scales(const float *k_scales, const float *v_scales, uint64_t count);
     // query: the type of q and out; the pool dtype for bf16/f16 pools, bf16

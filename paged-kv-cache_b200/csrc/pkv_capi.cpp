@@ -240,6 +240,16 @@ int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, vo
     return guarded("pkv_zero_blocks_dev", [&] { return b->impl->zero_blocks_dev(blocks, count, as_stream(stream)); });
 }
 
+int pkv_copy_zero_blocks_dev(pkv_backend *b, const int64_t *srcs, const int64_t *dst_offsets,
+                             const int64_t *dsts, const int64_t *zero_src, int64_t num_srcs,
+                             const int64_t *zero_ids, int64_t num_zero, void *stream) {
+    if (!b) return null_handle();
+    return guarded("pkv_copy_zero_blocks_dev", [&] {
+        return b->impl->copy_zero_dev(srcs, dst_offsets, dsts, zero_src, num_srcs, zero_ids,
+                                      num_zero, as_stream(stream));
+    });
+}
+
 int pkv_resolve_slots_dev(pkv_backend *b, const int32_t *block_tables, int64_t table_stride,
                           const int32_t *ctx_lens, const int32_t *new_lens, int64_t num_seqs,
                           int64_t num_tokens, int32_t *cu_seqlens, int64_t *slot_mapping,

@@ -85,6 +85,26 @@ struct ZeroLaunch {
     DevError *err;
 };
 
+// A step's copy-on-write pairs and freed blocks in one launch. The pairs
+// are grouped by source: source i is read once and written to
+// dsts[dst_off[i] .. dst_off[i + 1]), then zeroed when zero_src[i] is set
+// (the step frees it); zero_ids are the step's other freed blocks.
+struct CopyZeroLaunch {
+    void *k_pool;
+    void *v_pool;
+    long long num_layers;
+    long long num_blocks;
+    long long block_bytes;
+    const long long *srcs;      // [num_srcs]
+    const long long *dst_off;   // [num_srcs + 1]
+    const long long *dsts;      // [dst_off[num_srcs]]
+    const long long *zero_src;  // [num_srcs]: nonzero to zero the source after its copies
+    long long num_srcs;
+    const long long *zero_ids;  // [num_zero]
+    long long num_zero;
+    DevError *err;
+};
+
 struct ResolveLaunch {
     const int *tables;
     long long table_stride;
@@ -205,6 +225,7 @@ cudaError_t launch_copy_blocks(const CopyLaunch &a, cudaStream_t s);
 bool bulk_copy_supported(const CopyLaunch &a);
 cudaError_t launch_copy_blocks_bulk(const CopyLaunch &a, int sms, cudaStream_t s);
 cudaError_t launch_zero_blocks(const ZeroLaunch &a, cudaStream_t s);
+cudaError_t launch_copy_zero(const CopyZeroLaunch &a, cudaStream_t s);
 // zero_blocks through the bulk-copy engine (pkv_bulk_copy.cu).
 bool bulk_zero_supported(const ZeroLaunch &a);
 cudaError_t launch_zero_blocks_bulk(const ZeroLaunch &a, int sms, cudaStream_t s);

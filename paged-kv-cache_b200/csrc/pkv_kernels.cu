@@ -246,6 +246,85 @@ zero_blocks_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_
     }
 }
 
+// ---- copy_blocks + zero_blocks of one step, one launch ----------------------
+//
+// One CTA per (entry, layer, plane, chunk of kThreads * UNROLL vectors), as
+// copy_blocks_kernel. Entries [0, num_srcs) are sources: the CTA loads its
+// chunk of the source plane once, stores it to each of the source's
+// destinations and then, if the step frees the source, stores zeros over it
+// (the same thread loaded those addresses first, so the copy reads the old
+// contents). Entries past num_srcs zero one freed block each. Bad ids are
+// recorded (index: the position in dsts of the pair, or dst_off[num_srcs] +
+// the position in zero_ids) and skipped.
+
+template <typename V, int UNROLL>
+__global__ void __launch_bounds__(kThreads)
+copy_zero_kernel(char *__restrict__ kp, char *__restrict__ vp, long long pool_layer,
+                 long long block_bytes, const CopyZeroLaunch a, int num_layers, int chunks) {
+    long long x = blockIdx.x;
+    const int chunk = (int)(x % chunks);
+    x /= chunks;
+    const int plane = (int)(x & 1);
+    x >>= 1;
+    const int layer = (int)(x % num_layers);
+    const long long entry = x / num_layers;
+    const bool report = threadIdx.x == 0 && chunk == 0 && plane == 0 && layer == 0;
+    char *base = (plane ? vp : kp) + layer * pool_layer;
+    const long long nvec = block_bytes / (long long)sizeof(V);
+    const long long v0 = (long long)chunk * kThreads * UNROLL + threadIdx.x;
+    V z;
+    memset(&z, 0, sizeof(V));
+    if (entry >= a.num_srcs) {
+        const long long zi = entry - a.num_srcs;
+        const long long blk = __ldg(a.zero_ids + zi);
+        if (blk < 0 || blk >= a.num_blocks) {
+            if (report) record_error(a.err, kInvalidBlock, __ldg(a.dst_off + a.num_srcs) + zi);
+            return;
+        }
+        V *d = reinterpret_cast<V *>(base + blk * block_bytes);
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const long long i = v0 + (long long)u * kThreads;
+            if (i < nvec) __stcs(d + i, z);
+        }
+        return;
+    }
+    const long long src = __ldg(a.srcs + entry);
+    const long long d0 = __ldg(a.dst_off + entry), d1 = __ldg(a.dst_off + entry + 1);
+    if (src < 0 || src >= a.num_blocks) {
+        if (report) record_error(a.err, kInvalidBlock, d0);
+        return;
+    }
+    V *s = reinterpret_cast<V *>(base + src * block_bytes);
+    V r[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+        const long long i = v0 + (long long)u * kThreads;
+        if (i < nvec) r[u] = __ldcs(s + i);
+    }
+    for (long long d = d0; d < d1; ++d) {
+        const long long dst = __ldg(a.dsts + d);
+        if (dst < 0 || dst >= a.num_blocks) {
+            if (report) record_error(a.err, kInvalidBlock, d);
+            continue;
+        }
+        if (dst == src) continue;
+        V *o = reinterpret_cast<V *>(base + dst * block_bytes);
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const long long i = v0 + (long long)u * kThreads;
+            if (i < nvec) __stcs(o + i, r[u]);
+        }
+    }
+    if (__ldg(a.zero_src + entry)) {
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const long long i = v0 + (long long)u * kThreads;
+            if (i < nvec) __stcs(s + i, z);
+        }
+    }
+}
+
 // ---- copy_blocks / zero_blocks over small block planes ---------------------
 //
 // A head-sharded pool has small block planes (2 KiB per plane and layer at
@@ -823,6 +902,30 @@ cudaError_t zero_v(const ZeroLaunch &a, cudaStream_t st) {
     return cudaGetLastError();
 }
 }  // namespace
+
+cudaError_t launch_copy_zero(const CopyZeroLaunch &a, cudaStream_t st) {
+    const long long entries = a.num_srcs + a.num_zero;
+    if (entries <= 0 || a.num_layers <= 0 || a.block_bytes <= 0) return cudaSuccess;
+    const int vb = pick_vector_bytes(2, {a.block_bytes}, {a.k_pool, a.v_pool});
+    auto go = [&](auto vec) {
+        using V = decltype(vec);
+        constexpr int U = 4;
+        const long long nvec = a.block_bytes / (long long)sizeof(V);
+        const int chunks = (int)((nvec + kThreads * U - 1) / (kThreads * U));
+        const long long grid = entries * a.num_layers * 2 * chunks;
+        if (grid >= (1ll << 31)) return cudaErrorInvalidValue;
+        copy_zero_kernel<V, U><<<(unsigned)grid, kThreads, 0, st>>>(
+            static_cast<char *>(a.k_pool), static_cast<char *>(a.v_pool),
+            a.num_blocks * a.block_bytes, a.block_bytes, a, (int)a.num_layers, chunks);
+        return cudaGetLastError();
+    };
+    switch (vb) {
+        case 16: return go(uint4{});
+        case 8: return go(uint2{});
+        case 4: return go(0u);
+        default: return go((unsigned short)0);
+    }
+}
 
 cudaError_t launch_copy_blocks(const CopyLaunch &a, cudaStream_t st) {
     if (a.num_pairs <= 0 || a.num_layers <= 0 || a.block_bytes <= 0) return cudaSuccess;

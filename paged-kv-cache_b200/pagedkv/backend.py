@@ -247,6 +247,16 @@ class B200Backend:
         n = blocks.shape[0] if count is None else count
         _check(lib.pkv_zero_blocks_dev(self._h, _ptr(blocks), n, _stream_ptr(stream)))
 
+    def copy_zero_blocks_dev(self, srcs, dst_offsets, dsts, zero_src, zero_ids, num_srcs=None,
+                             num_zero=None, stream=None) -> None:
+        """One launch for a step's copies (grouped by source, see
+        pkv_copy_zero_blocks_dev) and the blocks it zeroes; int64 device tensors."""
+        ns = srcs.shape[0] if num_srcs is None else num_srcs
+        nz = zero_ids.shape[0] if num_zero is None else num_zero
+        _check(lib.pkv_copy_zero_blocks_dev(self._h, _ptr(srcs), _ptr(dst_offsets), _ptr(dsts),
+                                            _ptr(zero_src), ns, _ptr(zero_ids), nz,
+                                            _stream_ptr(stream)))
+
     def resolve_slots(self, block_tables, ctx_lens, new_lens, num_tokens: int, cu_out, slots_out,
                       stream=None) -> None:
         """Device slot resolution: block_tables [S][stride] int32, ctx/new int32 [S]."""

@@ -138,13 +138,44 @@ def copy_waves(copies: np.ndarray):
     return ordered, [(int(a), int(c)) for a, c in zip(starts, counts) if c]
 
 
+def group_copy_zero(copies: np.ndarray, zero: np.ndarray, token_blocks: np.ndarray):
+    """The arrays of one fused copy + zero launch (pkv_copy_zero_blocks_dev)
+    for a step whose copies form one wave, or None when the step needs the
+    two separate launches: a destination that is zeroed, or a zeroed block
+    that receives one of the step's tokens (zeroing runs before the token
+    writes in the fused form, after them in the separate one).
+
+    Returns (srcs, dst_offsets, dsts, zero_src, zero_only): the distinct
+    sources in order of first use, each one's destinations in pair order, a
+    flag for the sources the step frees, and the other freed blocks."""
+    copies = np.asarray(copies, np.int64).reshape(-1, 2)
+    zero = np.asarray(zero, np.int64)
+    if len(copies) == 0 or len(zero) == 0:
+        return None
+    if np.isin(copies[:, 1], zero).any() or np.isin(zero, token_blocks).any():
+        return None
+    srcs, first, inv = np.unique(copies[:, 0], return_index=True, return_inverse=True)
+    by_first = np.argsort(first, kind="stable")  # sources in order of first use
+    rank = np.empty_like(by_first)
+    rank[by_first] = np.arange(len(by_first))
+    group = rank[inv]
+    order = np.argsort(group, kind="stable")
+    dsts = np.ascontiguousarray(copies[order, 1])
+    offs = np.concatenate([[0], np.cumsum(np.bincount(group, minlength=len(srcs)))]).astype(np.int64)
+    srcs = np.ascontiguousarray(srcs[by_first])
+    zero_src = np.isin(srcs, zero).astype(np.int64)
+    zero_only = np.ascontiguousarray(zero[~np.isin(zero, srcs)])
+    return srcs, offs, dsts, zero_src, zero_only
+
+
 class DeviceStepper:
     """Runs StepPlans on `backend`. With timing=True each step also records
     CUDA events around its four phases; ``phase_ms()`` sums them."""
 
     PHASES = ("copy_blocks", "resolve_and_cache", "reshape_and_cache", "zero_blocks")
 
-    def __init__(self, backend: B200Backend, stream=None, timing: bool = False):
+    def __init__(self, backend: B200Backend, stream=None, timing: bool = False,
+                 fuse_copy_zero: bool = True):
         import torch
 
         self.torch = torch
@@ -157,6 +188,10 @@ class DeviceStepper:
         self.launches = 0
         self.timing = timing
         self.events: list[list] = []
+        # Steps whose copies form one wave and whose zeroes touch neither a
+        # destination nor a written block run copies and zeroes as one launch.
+        self.fuse_copy_zero = fuse_copy_zero
+        self.fused_steps = 0
 
     def _mark(self, marks: list) -> None:
         if self.timing:
@@ -193,25 +228,51 @@ class DeviceStepper:
     def prepare(self, plan: StepPlan) -> "Prepared":
         """Host-side work of a step done ahead of time: copy waves and one
         packed buffer of every array the device needs."""
-        return Prepared(plan)
+        return Prepared(plan, self.b.config().block_size, self.fuse_copy_zero)
+
+    def make_resident(self, prepared: list["Prepared"]):
+        """Uploads the metadata of every prepared step into one device buffer
+        (for replaying a trace whose inputs are already in HBM); returns the
+        buffer, which must outlive the steps' apply()."""
+        torch = self.torch
+        total = sum(p.packed.size for p in prepared)
+        buf = torch.empty(max(total, 1), dtype=torch.int64, device=self.dev)
+        host = torch.from_numpy(np.concatenate([p.packed for p in prepared]) if prepared else
+                                np.zeros(1, np.int64))
+        buf[:host.numel()].copy_(host)
+        off = 0
+        for p in prepared:
+            p.resident = buf[off:off + p.packed.size]
+            off += p.packed.size
+        return buf
 
     def apply(self, plan, k, v) -> int:
         """Runs one step (a StepPlan, or one made ready by prepare()). k, v:
         device [L][R][entry] rows; token i of the step reads row i % R
         (R >= the step's token count keeps every row distinct)."""
         torch = self.torch
-        p = plan if isinstance(plan, Prepared) else Prepared(plan)
+        p = plan if isinstance(plan, Prepared) else self.prepare(plan)
         b, st = self.b, self.stream
         tr, d, t, s = p.tr, p.d, p.t, p.s
         self._ensure(t, s)
-        dev = self.stage.upload_packed(p.packed, st)
-        d_copies, d_tables, d_ctx, d_new, d_direct, d_zero = (dev[a:c] for a, c in p.spans)
+        # A step made resident (make_resident) reads its metadata where it
+        # already lies on the device; otherwise it is uploaded now.
+        dev = p.resident if p.resident is not None else self.stage.upload_packed(p.packed, st)
+        d_copies, d_tables, d_ctx, d_new, d_direct, d_zero = (dev[a:c] for a, c in p.spans[:6])
         n = 0
         marks: list = []
         self._mark(marks)
-        for start, count in p.waves:
-            b.copy_blocks_dev(d_copies[2 * start:], count=count, stream=st)
+        if p.fused is not None:  # copies and zeroes in one launch
+            d_srcs, d_off, d_dsts, d_zsrc, d_zonly = (dev[a:c] for a, c in p.spans[6:])
+            ns, nz = p.fused
+            b.copy_zero_blocks_dev(d_srcs, d_off, d_dsts, d_zsrc, d_zonly, num_srcs=ns,
+                                   num_zero=nz, stream=st)
             n += 1
+            self.fused_steps += 1
+        else:
+            for start, count in p.waves:
+                b.copy_blocks_dev(d_copies[2 * start:], count=count, stream=st)
+                n += 1
         self._mark(marks)
         rows = k.shape[1]
         fused = s and tr <= rows and k.dtype == v.dtype and _pool_dtype_matches(b, k)
@@ -245,7 +306,7 @@ class DeviceStepper:
             n += 1
             start += c
         self._mark(marks)
-        if p.nzero:
+        if p.nzero and p.fused is None:
             b.zero_blocks_dev(d_zero, count=p.nzero, stream=st)
             n += 1
         self._mark(marks)
@@ -256,16 +317,26 @@ class DeviceStepper:
 
 
 class Prepared:
-    """A StepPlan with its host-side work done: copy waves computed and every
+    """A StepPlan with its host-side work done: copy waves computed (or the
+    copies grouped by source for one fused copy + zero launch) and every
     array packed, as 8-byte-aligned int64 words, into one buffer."""
 
-    def __init__(self, plan: StepPlan):
+    def __init__(self, plan: StepPlan, block_size: int = 16, fuse_copy_zero: bool = True):
         tables = np.ascontiguousarray(plan.tables, np.int32)
         copies, self.waves = copy_waves(plan.copies)
+        self.fused = None
+        extra = []
+        if fuse_copy_zero and len(self.waves) == 1 and len(plan.zero):
+            written = np.concatenate([np.unique(tables[tables >= 0]).astype(np.int64),
+                                      np.asarray(plan.direct_slots, np.int64) // block_size])
+            g = group_copy_zero(copies, plan.zero, written)
+            if g is not None:
+                extra = list(g)
+                self.fused = (len(g[0]), len(g[4]))
         parts = [copies, tables, np.ascontiguousarray(plan.ctx, np.int32),
                  np.ascontiguousarray(plan.new, np.int32),
                  np.ascontiguousarray(plan.direct_slots, np.int64),
-                 np.ascontiguousarray(plan.zero, np.int64)]
+                 np.ascontiguousarray(plan.zero, np.int64), *extra]
         words = [(a.nbytes + 7) // 8 for a in parts]
         self.packed = np.zeros(max(sum(words), 1), np.int64)
         raw = self.packed.view(np.uint8)
@@ -278,3 +349,4 @@ class Prepared:
         self.t, self.s = self.tr + self.d, len(plan.new)
         self.table_shape, self.table_elems = tables.shape, tables.size
         self.nzero = len(plan.zero)
+        self.resident = None  # device view of `packed`, once made resident

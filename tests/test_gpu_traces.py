@@ -59,12 +59,12 @@ def assert_same_pool(gpu, cpu):
     np.testing.assert_array_equal(gv.view(np.uint32), ov.view(np.uint32))
 
 
-def run(cfg, plans, r=2048, check_every=0):
+def run(cfg, plans, r=2048, check_every=0, fuse=True, fused_steps=None):
     import torch
 
     gpu, cpu = B200Backend(cfg, dtype="bf16"), OracleBackend(cfg)
     k, v, kf, vf = rows(cfg, r, 9)
-    stepper = DeviceStepper(gpu)
+    stepper = DeviceStepper(gpu, fuse_copy_zero=fuse)
     stats = []
     for i, plan in enumerate(plans):
         stepper.apply(plan, k, v)
@@ -77,6 +77,8 @@ def run(cfg, plans, r=2048, check_every=0):
     assert gpu.device_error() is None
     assert_same_pool(gpu, cpu)
     assert gpu.digest() == cpu.digest()
+    if fused_steps is not None:
+        fused_steps.append(stepper.fused_steps)
     return stats
 
 
@@ -95,15 +97,24 @@ def test_ragged_prefill_chunk(cuda):  # config 3 at reduced geometry
     run(cfg, [plan_from_batch(batch)], r=4096)
 
 
+@pytest.mark.parametrize("fuse", [True, False])
 @pytest.mark.parametrize("interleave", [False, True])
-def test_beam_search_copy_on_write_trace(cuda, interleave):  # config 4 at reduced geometry
+def test_beam_search_copy_on_write_trace(cuda, interleave, fuse):  # config 4 at reduced geometry
     """interleave=True frees old beams group by group, which chains copy
-    pairs within a step; the driver must keep their sequential meaning."""
+    pairs within a step; the driver must keep their sequential meaning.
+    fuse=True runs each eligible step's copies and zeroes as one launch
+    (sources grouped, freed sources zeroed after their copies); with one
+    wave of copies per step every step with zeroes is eligible."""
     cfg = CacheConfig(num_blocks=512, block_size=8, num_kv_heads=2, head_dim=16, num_layers=3,
                       dtype_bytes=2)
     plans = list(beam_cow_trace(cfg, groups=6, width=4, prefix=37, steps=30, zero_per_step=5, seed=2,
                                 interleave=interleave))
-    stats = run(cfg, plans, r=512, check_every=7)
+    fused = []
+    stats = run(cfg, plans, r=512, check_every=7, fuse=fuse, fused_steps=fused)
+    if fuse and not interleave:
+        assert fused[0] > 20
+    if not fuse:
+        assert fused[0] == 0
     copies = sum(s["copies"] for s in stats)
     # Every child pays a copy except on steps whose append opens a new block.
     assert copies == sum(24 for s in range(1, 31) if (37 + s - 1) % 8 != 0)
