@@ -927,17 +927,20 @@ def wl_trace(run, kind: str) -> dict:
     }
     fused = stepper.fused_steps
     out["config"]["fused_copy_zero_steps"] = fused
-    if kind == "cow" and fused == len(timed):
-        # Every step ran its copies and zeroes as one launch: that launch's
-        # bytes are the copies' and the zeroes'.
+    if kind == "cow" and fused:
+        # Steps that ran their copies and zeroes as one launch move both in
+        # the copy phase; the others zero in their own phase.
+        fz = sum(len(p_.zero) for p_, q_ in zip(timed, prepared) if q_.fused is not None)
+        cz_bytes = copy_bytes + fz * L * 2 * bb + 8 * fz
+        rest_zero = zero_bytes - (fz * L * 2 * bb + 8 * fz)
         out["roofline"] = roofline("copy_zero_kernel (256 copy-on-write pairs grouped by source "
                                    "+ 64 freed blocks zeroed, 28 layers, one launch per step)",
-                                   (copy_bytes + zero_bytes) / len(timed),
-                                   phase["copy_blocks"] / len(timed),
+                                   cz_bytes / len(timed), phase["copy_blocks"] / len(timed),
                                    profile_traffic("copy_zero_cow_ncu"))
-        out["phase_gb_per_s"]["copy_blocks"] = ((copy_bytes + zero_bytes) /
-                                                (phase["copy_blocks"] / 1e3) / 1e9)
-        out["phase_gb_per_s"]["zero_blocks"] = None
+        out["roofline"]["fused_steps"] = fused
+        out["phase_gb_per_s"]["copy_blocks"] = cz_bytes / (phase["copy_blocks"] / 1e3) / 1e9
+        out["phase_gb_per_s"]["zero_blocks"] = (rest_zero / (phase["zero_blocks"] / 1e3) / 1e9
+                                                if rest_zero and phase["zero_blocks"] else None)
     elif kind == "cow":
         kern = "copy_blocks_bulk_kernel" if args.copy_engine == "bulk" else "copy_blocks_kernel"
         out["roofline"] = roofline(f"{kern} (256 pairs x 28 layers per step)",
