@@ -126,3 +126,42 @@ def test_a_rank_that_dies_is_detected_by_the_survivor(tmp_path):
     assert not alive, "a surviving rank hung instead of failing"
     assert procs[1].exitcode == 3
     assert Path(tmp_path, "rank0.txt").read_text().startswith("error")
+
+
+def _breakdown_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    """bench.py's per-rank view of a multi-GPU trace, over gloo on CPU: each
+    rank contributes its per-step device times and token-write time."""
+    sys.path[:0] = [str(ROOT / "paged-kv-cache_b200"), str(ROOT)]
+    import json
+    import types
+
+    import torch
+    import torch.distributed as dist
+
+    import bench
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    run = types.SimpleNamespace(torch=torch, dist=dist, world=world, rank=rank,
+                                dev=torch.device("cpu"))
+    # Rank 1 is slower on steps 1 and 3; rank 0 on steps 0, 2 and 4.
+    steps = [2.0, 1.0, 2.0, 1.0, 2.0] if rank == 0 else [1.0, 3.0, 1.0, 3.0, 1.0]
+    out = bench.rank_breakdown(run, steps, write_bytes=6.55e9, write_ms=1000.0 * (1 + rank))
+    Path(out_dir, f"rank{rank}.json").write_text(json.dumps(out))
+    dist.destroy_process_group()
+
+
+def test_rank_breakdown_over_two_gloo_ranks(tmp_path):
+    import json
+
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_breakdown_rank_main, args=(2, 29534, str(tmp_path)), nprocs=2,
+                       start_method="spawn", join=True)
+    outs = [json.loads(Path(tmp_path, f"rank{r}.json").read_text()) for r in range(2)]
+    assert outs[0] == outs[1]  # every rank computes the same view
+    o = outs[0]
+    assert o["device_ms_per_rank"] == [8.0, 9.0]
+    assert o["steps_bounded_by_rank"] == [3, 2]
+    fr = o["token_write_frac_of_peak_per_rank"]
+    assert abs(fr[0] / fr[1] - 2.0) < 1e-9  # rank 1 took twice as long for the same bytes
