@@ -243,6 +243,12 @@ class Run:
             raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {self.world}")
         torch.cuda.set_device(self.local)
         self.dev = torch.device("cuda", self.local)
+        # The ranks of one box share its host cores: give each rank's host
+        # stager (the e2e paths) its share instead of one thread per core each.
+        local_world = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+        if local_world > 1:
+            os.environ.setdefault("PKV_HOST_THREADS",
+                                  str(max(1, (os.cpu_count() or 1) // local_world)))
         if self.world > 1:
             from datetime import timedelta
 
