@@ -14,14 +14,21 @@ from pagedkv.workloads import Stream
 pytestmark = pytest.mark.gpu
 
 
-def filled(cfg, seed, shards=(0, 1)):
+def filled(cfg, seed, shards=(0, 1), dtype="bf16"):
     import torch
 
-    b = B200Backend(cfg, dtype="bf16", shard_rank=shards[0], num_shards=shards[1])
+    b = B200Backend(cfg, dtype=dtype, shard_rank=shards[0], num_shards=shards[1])
     g = torch.Generator(device="cuda").manual_seed(seed)
     for p in b.planes():
-        p.copy_(torch.randn(p.shape, generator=g, device="cuda").to(torch.bfloat16))
+        x = torch.randn(p.shape, generator=g, device="cuda")
+        p.copy_(x.to(torch.float8_e4m3fn).view(torch.uint8) if dtype == "fp8_e4m3" else x.to(p.dtype))
     return b
+
+
+def bits(p):
+    import torch
+
+    return p.view(torch.uint8) if p.element_size() == 1 else p.view(torch.int16)
 
 
 def dev(x):
@@ -30,12 +37,14 @@ def dev(x):
     return torch.from_numpy(np.ascontiguousarray(x, np.int64)).cuda()
 
 
-@pytest.mark.parametrize("heads,shards", [(4, 1), (4, 8), (3, 1)])
-def test_fused_launch_equals_copy_then_zero(cuda, heads, shards):
+@pytest.mark.parametrize("heads,shards,dtype", [(4, 1, "bf16"), (4, 8, "bf16"), (3, 1, "bf16"),
+                                                (4, 1, "f32"), (4, 2, "fp8_e4m3"), (1, 1, "f16")])
+def test_fused_launch_equals_copy_then_zero(cuda, heads, shards, dtype):
     import torch
 
+    nbytes = {"bf16": 2, "f16": 2, "f32": 4, "fp8_e4m3": 1}[dtype]
     cfg = CacheConfig(num_blocks=600, block_size=16, num_kv_heads=heads, head_dim=128,
-                      num_layers=5, dtype_bytes=2)
+                      num_layers=5, dtype_bytes=nbytes)
     st = Stream(heads * 10 + shards)
     ids = st.permutation(cfg.num_blocks)
     srcs = ids[:40]
@@ -45,16 +54,20 @@ def test_fused_launch_equals_copy_then_zero(cuda, heads, shards):
     zero = np.concatenate([srcs[:25], ids[300:340]]).astype(np.int64)
     g = group_copy_zero(copies, zero, np.zeros(0, np.int64))
     assert g is not None and g[3].sum() > 0
-    a = filled(cfg, 7, (0, shards))
-    b = filled(cfg, 7, (0, shards))
+    a = filled(cfg, 7, (0, shards), dtype)
+    b = filled(cfg, 7, (0, shards), dtype)
     a.copy_blocks_dev(dev(copies))
     a.zero_blocks_dev(dev(zero))
     b.copy_zero_blocks_dev(*(dev(x) for x in g))
     torch.cuda.synchronize()
     assert a.device_error() is None and b.device_error() is None
     for x, y in zip(a.planes(), b.planes()):
-        assert torch.equal(x.view(torch.int16), y.view(torch.int16))
-    assert int(torch.count_nonzero(b.planes()[0][:, dev(zero)])) == 0
+        assert torch.equal(bits(x), bits(y))
+    assert int(torch.count_nonzero(bits(b.planes()[0])[:, dev(zero)])) == 0
+    # Every destination holds its source's plane as it was before the step.
+    ref = filled(cfg, 7, (0, shards), dtype)
+    for p_new, p_old in zip(b.planes(), ref.planes()):
+        assert torch.equal(bits(p_new)[:, dev(copies[:, 1])], bits(p_old)[:, dev(copies[:, 0])])
 
 
 def test_bad_ids_are_recorded_and_skipped(cuda):
