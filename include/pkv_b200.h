@@ -244,6 +244,25 @@ int pkv_resolve_and_cache_dev(pkv_backend *b, const int32_t *block_tables, int64
                               int64_t layer, const void *k, const void *v,
                               int64_t src_token_stride, int64_t src_layer_stride, int src_dtype,
                               void *stream);
+/* One scheduler step's whole cache write in one launch (no counterpart in
+ * the reference; its StepOutcome carries both kinds of token,
+ * crates/paged-kv-core/src/scheduler.rs:57-86): the num_tokens tokens of the
+ * sequences given by block tables (admitted prompts), resolved as
+ * pkv_resolve_and_cache_dev does, then num_direct tokens whose slots the
+ * host already has (decoded tokens: direct_slots, int64, device memory;
+ * negative skipped, past the pool recorded as InvalidBlock at the token's
+ * index). k and v hold num_tokens + num_direct rows, the resolved tokens'
+ * first. Equivalent to pkv_resolve_and_cache_dev followed by
+ * pkv_reshape_and_cache_dev of the direct tokens; pools of the source's
+ * type only (an fp8 pool is refused). slot_mapping, if given, receives the
+ * resolved tokens' slots. */
+int pkv_resolve_and_cache_mixed_dev(pkv_backend *b, const int32_t *block_tables,
+                                    int64_t table_stride, const int32_t *ctx_lens,
+                                    const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
+                                    int32_t *cu_seqlens, int64_t *slot_mapping,
+                                    const int64_t *direct_slots, int64_t num_direct, int64_t layer,
+                                    const void *k, const void *v, int64_t src_token_stride,
+                                    int64_t src_layer_stride, int src_dtype, void *stream);
 /* Decode attention over layer `layer` of the pool: one query token per
  * sequence. No counterpart in the reference, which leaves paged_attention
  * off its trait until its signature is settled

@@ -912,7 +912,8 @@ Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_s
                                           int64_t num_seqs, int64_t num_tokens, int32_t *cu,
                                           int64_t *slots_out, int64_t layer, const void *k,
                                           const void *v, int64_t tok_stride,
-                                          int64_t layer_stride, DType src, cudaStream_t st) {
+                                          int64_t layer_stride, DType src, cudaStream_t st,
+                                          const int64_t *direct_slots, int64_t num_direct) {
     if (layer < -1 || (layer >= 0 && (uint64_t)layer >= cfg_.num_layers))
         return error(PKV_ERR_INVALID_LAYER, layer, (int64_t)cfg_.num_layers,
                      msg_layer((uint64_t)layer, cfg_.num_layers));
@@ -934,17 +935,28 @@ Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_s
                      "the fused path moves bytes, or quantises into an fp8 pool: source dtype "
                      "must equal the pool dtype (use pkv_resolve_slots_dev + "
                      "pkv_reshape_and_cache_dev to convert)");
+    if (num_direct < 0)
+        return error(PKV_ERR_SHAPE_MISMATCH, 0, num_direct, "negative direct token count");
+    if (num_direct > 0 && quantise)
+        return error(PKV_ERR_DEVICE, 0, 0,
+                     "host-slot tokens in the fused step are for pools of the source's type; "
+                     "an fp8 pool takes them through pkv_reshape_and_cache_dev");
+    if (num_tokens + num_direct > std::numeric_limits<int32_t>::max())
+        return error(PKV_ERR_SHAPE_MISMATCH, std::numeric_limits<int32_t>::max(),
+                     num_tokens + num_direct, "too many tokens for one step");
     if (!cu || (num_seqs > 0 && (!ctx || !new_lens)) ||
-        (num_tokens > 0 && (!tables || !k || !v)))
+        (num_tokens > 0 && (!tables || !k || !v)) ||
+        (num_direct > 0 && (!direct_slots || !k || !v)))
         return error(PKV_ERR_DEVICE, 0, 0, "null device pointer");
+    const int64_t rows = num_tokens + num_direct;  // source rows the launch reads
     if (tok_stride <= 0) tok_stride = (int64_t)shard_entry_;
     if ((uint64_t)tok_stride < shard_entry_)
         return error(PKV_ERR_SHAPE_MISMATCH, (int64_t)shard_entry_, tok_stride,
                      "token stride shorter than an entry");
     const bool all = layer == -1;
-    if (all && layer_stride <= 0) layer_stride = tok_stride * num_tokens;
-    if (all && layer_stride < tok_stride * num_tokens)
-        return error(PKV_ERR_SHAPE_MISMATCH, tok_stride * num_tokens, layer_stride,
+    if (all && layer_stride <= 0) layer_stride = tok_stride * rows;
+    if (all && layer_stride < tok_stride * rows)
+        return error(PKV_ERR_SHAPE_MISMATCH, tok_stride * rows, layer_stride,
                      "layer stride shorter than a layer's rows");
     DeviceGuard g(device_);
     const int es = dtype_size(src);
@@ -970,6 +982,8 @@ Status B200Backend::resolve_and_cache_dev(const int32_t *tables, int64_t table_s
     a.slots_per_layer = (long long)slots_per_layer();
     a.entry_bytes = (long long)entry_bytes();
     a.err = d_err_;
+    a.direct_slots = reinterpret_cast<const long long *>(direct_slots);
+    a.num_direct = num_direct;
     if (quantise) {
         a.src_dtype = src;
         a.pool_dtype = dtype_;

@@ -111,7 +111,8 @@ class B200Backend {
                                  const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
                                  int32_t *cu, int64_t *slots_out, int64_t layer, const void *k,
                                  const void *v, int64_t tok_stride, int64_t layer_stride,
-                                 DType src, cudaStream_t s);
+                                 DType src, cudaStream_t s, const int64_t *direct_slots = nullptr,
+                                 int64_t num_direct = 0);
     Status digest(uint64_t *k, uint64_t *v, cudaStream_t s);
     Status digest_rows(int64_t layer, const void *k, const void *v, int64_t tok_stride,
                        int64_t layer_stride, const int64_t *slots, int64_t num_tokens, DType src,

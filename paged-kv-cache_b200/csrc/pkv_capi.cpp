@@ -240,6 +240,24 @@ int pkv_zero_blocks_dev(pkv_backend *b, const int64_t *blocks, int64_t count, vo
     return guarded("pkv_zero_blocks_dev", [&] { return b->impl->zero_blocks_dev(blocks, count, as_stream(stream)); });
 }
 
+int pkv_resolve_and_cache_mixed_dev(pkv_backend *b, const int32_t *block_tables,
+                                    int64_t table_stride, const int32_t *ctx_lens,
+                                    const int32_t *new_lens, int64_t num_seqs, int64_t num_tokens,
+                                    int32_t *cu_seqlens, int64_t *slot_mapping,
+                                    const int64_t *direct_slots, int64_t num_direct, int64_t layer,
+                                    const void *k, const void *v, int64_t src_token_stride,
+                                    int64_t src_layer_stride, int src_dtype, void *stream) {
+    if (!b) return null_handle();
+    if (!valid_dtype(src_dtype)) return bad_dtype();
+    return guarded("pkv_resolve_and_cache_mixed_dev", [&] {
+        return b->impl->resolve_and_cache_dev(block_tables, table_stride, ctx_lens, new_lens,
+                                              num_seqs, num_tokens, cu_seqlens, slot_mapping,
+                                              layer, k, v, src_token_stride, src_layer_stride,
+                                              static_cast<pkv::DType>(src_dtype),
+                                              as_stream(stream), direct_slots, num_direct);
+    });
+}
+
 int pkv_copy_zero_blocks_dev(pkv_backend *b, const int64_t *srcs, const int64_t *dst_offsets,
                              const int64_t *dsts, const int64_t *zero_src, int64_t num_srcs,
                              const int64_t *zero_ids, int64_t num_zero, void *stream) {

@@ -158,6 +158,11 @@ struct ResolveCacheLaunch {
     DType pool_dtype = DType::F32;
     long long entry_elems = 0;
     Fp8Scales fp8;
+    // Tokens whose slots the host already knows (a step's decoded tokens),
+    // after the resolved ones: token num_tokens + j reads source row
+    // num_tokens + j and goes to direct_slots[j] (negative: skipped).
+    const long long *direct_slots = nullptr;
+    long long num_direct = 0;
 };
 
 // Digest of rows as a scatter into an empty pool would store them.

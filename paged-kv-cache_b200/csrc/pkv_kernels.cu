@@ -538,15 +538,24 @@ __device__ __forceinline__ void resolve_cache_general(const ResolveCacheLaunch &
     const char *vbase = static_cast<const char *>(a.v);
     char *kp = static_cast<char *>(a.k_pool) + a.first_layer * pool_layer;
     char *vp = static_cast<char *>(a.v_pool) + a.first_layer * pool_layer;
-    const long long total = a.num_tokens * nvec;
+    const long long total = (a.num_tokens + a.num_direct) * nvec;
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x; it < total; it += stride) {
         const long long t = it / nvec;
         const int vec = (int)(it - t * nvec);
         const bool lead = vec == 0 && blockIdx.y == 0;
-        const long long s = slot_of_token(t, s_cu, (int)a.num_seqs, a.ctx_lens, a.tables,
-                                          a.table_stride, a.block_size, a.num_blocks, a.err, lead);
-        if (lead && a.slots_out) a.slots_out[t] = s;
+        long long s;
+        if (t < a.num_tokens) {
+            s = slot_of_token(t, s_cu, (int)a.num_seqs, a.ctx_lens, a.tables, a.table_stride,
+                              a.block_size, a.num_blocks, a.err, lead);
+            if (lead && a.slots_out) a.slots_out[t] = s;
+        } else {  // a host-known slot, as reshape_copy_kernel takes it
+            s = __ldg(a.direct_slots + (t - a.num_tokens));
+            if (s >= a.slots_per_layer) {
+                if (lead) record_error(a.err, kInvalidBlock, t);
+                continue;
+            }
+        }
         if (s < 0) continue;
         const long long col = (long long)vec * sizeof(V);
         const char *ks = kbase + t * src_tok + l0 * src_layer + col;
@@ -1031,7 +1040,7 @@ template <typename V>
 cudaError_t resolve_cache_v(const ResolveCacheLaunch &a, long long entry_bytes, int sms,
                             cudaStream_t st) {
     const int nvec = (int)(entry_bytes / (long long)sizeof(V));
-    const long long items = a.num_tokens * nvec;
+    const long long items = (a.num_tokens + a.num_direct) * nvec;
     long long chunks;
     const int lpc = layers_per_chunk(items, a.num_layers, sms, &chunks);
     long long bx = std::min<long long>((items + kThreads - 1) / kThreads, (long long)sms * 256);
@@ -1045,7 +1054,8 @@ cudaError_t resolve_cache_v(const ResolveCacheLaunch &a, long long entry_bytes, 
     const bool one_wave = (long long)grid.x * grid.y <= (long long)sms * 4;
     // One new token per sequence with every item in the first pass of the
     // grid: the decode form, which skips the scan when the lengths allow.
-    const bool decode = a.num_tokens == a.num_seqs && (long long)bx * kThreads >= items;
+    const bool decode = a.num_tokens == a.num_seqs && a.num_direct == 0 &&
+                        (long long)bx * kThreads >= items;
     auto kern = decode ? resolve_cache_decode_kernel<V, 4>
                 : one_wave ? resolve_cache_kernel<V, 4, 4> : resolve_cache_kernel<V, 4, 2>;
     const size_t smem = (size_t)(a.num_seqs + 1) * sizeof(int);

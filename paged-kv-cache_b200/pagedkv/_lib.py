@@ -65,6 +65,8 @@ _PROTOS = {
     "pkv_copy_blocks_dev": (_I, [_P, _P, _I64, _P]),
     "pkv_zero_blocks_dev": (_I, [_P, _P, _I64, _P]),
     "pkv_copy_zero_blocks_dev": (_I, [_P, _P, _P, _P, _P, _I64, _P, _I64, _P]),
+    "pkv_resolve_and_cache_mixed_dev": (_I, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64,
+                                             _I64, _P, _P, _I64, _I64, _I, _P]),
     "pkv_set_copy_engine": (_I, [_P, _I]),
     "pkv_set_kv_scales": (_I, [_P, _P, _P, _U64]),
     "pkv_paged_attention_dev": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, C.c_float,

@@ -283,6 +283,24 @@ class B200Backend:
                                              _ptr(slots_out), lay, _ptr(k), _ptr(v), tok_stride,
                                              layer_stride, tag, _stream_ptr(stream)))
 
+    def resolve_and_cache_mixed(self, block_tables, ctx_lens, new_lens, num_tokens: int, cu_out,
+                                direct_slots, num_direct: int, k, v, layer: int | None = None,
+                                slots_out=None, stream=None) -> None:
+        """One launch for a step's resolved tokens (rows [0, num_tokens)) and
+        its host-slot tokens (rows num_tokens + j to direct_slots[j])."""
+        s = ctx_lens.shape[0]
+        stride = block_tables.shape[1] if block_tables.dim() == 2 else 0
+        tag = _torch_tag(k)
+        _same_layout(k, v)
+        if layer is None:
+            tok_stride, layer_stride, lay = k.stride(1), k.stride(0), -1
+        else:
+            tok_stride, layer_stride, lay = k.stride(0), 0, layer
+        _check(lib.pkv_resolve_and_cache_mixed_dev(
+            self._h, _ptr(block_tables), stride, _ptr(ctx_lens), _ptr(new_lens), s, num_tokens,
+            _ptr(cu_out), _ptr(slots_out), _ptr(direct_slots), num_direct, lay, _ptr(k), _ptr(v),
+            tok_stride, layer_stride, tag, _stream_ptr(stream)))
+
     def paged_attention_plan(self, context_lens, max_context_len: int, stream=None) -> None:
         """Longest-first order of the sequences for the following
         paged_attention calls with these context_lens

@@ -175,7 +175,7 @@ class DeviceStepper:
     PHASES = ("copy_blocks", "resolve_and_cache", "reshape_and_cache", "zero_blocks")
 
     def __init__(self, backend: B200Backend, stream=None, timing: bool = False,
-                 fuse_copy_zero: bool = True):
+                 fuse_copy_zero: bool = True, fuse_mixed: bool = True):
         import torch
 
         self.torch = torch
@@ -192,6 +192,10 @@ class DeviceStepper:
         # destination nor a written block run copies and zeroes as one launch.
         self.fuse_copy_zero = fuse_copy_zero
         self.fused_steps = 0
+        # Steps with both resolved and host-slot tokens write them in one
+        # launch when the rows do not wrap.
+        self.fuse_mixed = fuse_mixed
+        self.mixed_steps = 0
 
     def _mark(self, marks: list) -> None:
         if self.timing:
@@ -276,7 +280,16 @@ class DeviceStepper:
         self._mark(marks)
         rows = k.shape[1]
         fused = s and tr <= rows and k.dtype == v.dtype and _pool_dtype_matches(b, k)
-        if fused:
+        mixed = fused and d and t <= rows and self.fuse_mixed
+        if mixed:
+            # Resolved and host-slot tokens in one launch: token i reads row i.
+            b.resolve_and_cache_mixed(d_tables.view(torch.int32)[: p.table_elems].view(p.table_shape),
+                                      d_ctx.view(torch.int32)[:s], d_new.view(torch.int32)[:s], tr,
+                                      self.cu, d_direct, d, k[:, :t], v[:, :t],
+                                      slots_out=self.slots[:tr], stream=st)
+            n += 1
+            self.mixed_steps += 1
+        elif fused:
             # Slots resolved inline by the scatter itself; they are also
             # published into self.slots for later readers of the cache.
             b.resolve_and_cache(d_tables.view(torch.int32)[: p.table_elems].view(p.table_shape),
@@ -293,7 +306,7 @@ class DeviceStepper:
         # Token i reads row i % rows: scatter in runs that do not wrap. Tokens
         # past the resolved ones take their slots straight from the uploaded
         # list; after a separate resolution every slot is in self.slots.
-        start = tr if fused or not s else 0
+        start = t if mixed else (tr if fused or not s else 0)
         if not fused and s and d:
             with torch.cuda.stream(st):
                 self.slots[tr:t].copy_(d_direct[:d], non_blocking=True)

@@ -21,7 +21,7 @@ def filled(cfg, seed, shards=(0, 1), dtype="bf16"):
     g = torch.Generator(device="cuda").manual_seed(seed)
     for p in b.planes():
         x = torch.randn(p.shape, generator=g, device="cuda")
-        p.copy_(x.to(torch.float8_e4m3fn).view(torch.uint8) if dtype == "fp8_e4m3" else x.to(p.dtype))
+        p.copy_(x.to(p.dtype))
     return b
 
 

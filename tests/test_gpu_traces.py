@@ -59,12 +59,12 @@ def assert_same_pool(gpu, cpu):
     np.testing.assert_array_equal(gv.view(np.uint32), ov.view(np.uint32))
 
 
-def run(cfg, plans, r=2048, check_every=0, fuse=True, fused_steps=None):
+def run(cfg, plans, r=2048, check_every=0, fuse=True, fused_steps=None, mixed_steps=None):
     import torch
 
     gpu, cpu = B200Backend(cfg, dtype="bf16"), OracleBackend(cfg)
     k, v, kf, vf = rows(cfg, r, 9)
-    stepper = DeviceStepper(gpu, fuse_copy_zero=fuse)
+    stepper = DeviceStepper(gpu, fuse_copy_zero=fuse, fuse_mixed=fuse)
     stats = []
     for i, plan in enumerate(plans):
         stepper.apply(plan, k, v)
@@ -79,6 +79,8 @@ def run(cfg, plans, r=2048, check_every=0, fuse=True, fused_steps=None):
     assert gpu.digest() == cpu.digest()
     if fused_steps is not None:
         fused_steps.append(stepper.fused_steps)
+    if mixed_steps is not None:
+        mixed_steps.append(stepper.mixed_steps)
     return stats
 
 
@@ -120,13 +122,19 @@ def test_beam_search_copy_on_write_trace(cuda, interleave, fuse):  # config 4 at
     assert copies == sum(24 for s in range(1, 31) if (37 + s - 1) % 8 != 0)
 
 
+@pytest.mark.parametrize("fuse", [True, False])
 @pytest.mark.parametrize("fork_rate", [0.0, 0.5])
-def test_continuous_batching_churn_trace(cuda, fork_rate):  # config 5 at reduced geometry
+def test_continuous_batching_churn_trace(cuda, fork_rate, fuse):  # config 5 at reduced geometry
+    """fuse=True writes a step's admitted prompts and decoded tokens in one
+    launch (pkv_resolve_and_cache_mixed_dev) and its copies and zeroes in
+    another, where the step allows; fuse=False issues every part apart."""
     cfg = CacheConfig(num_blocks=96, block_size=4, num_kv_heads=2, head_dim=16, num_layers=2,
                       dtype_bytes=2)
     plans = list(churn_trace(cfg, steps=250, arrival_rate=1.2, prompt_lo=2, prompt_hi=60,
                              out_mean=12.0, max_batch=24, fork_rate=fork_rate, seed=5))
-    stats = run(cfg, plans, r=1024, check_every=50)
+    mixed = []
+    stats = run(cfg, plans, r=1024, check_every=50, fuse=fuse, mixed_steps=mixed)
+    assert (mixed[0] > 50) if fuse else (mixed[0] == 0)
     assert sum(s["preempted"] for s in stats) > 0
     assert sum(s["finished"] for s in stats) > 100
     if fork_rate:
