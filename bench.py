@@ -70,7 +70,8 @@ def parse():
                    help="attention: also time flashinfer's paged decode (tensor-core path) on "
                         "the same pool, for comparison")
     p.add_argument("--no-fuse", action="store_true",
-                   help="cow/churn: copy_blocks and zero_blocks as two launches per step")
+                   help="cow/churn: copy_blocks and zero_blocks as two launches per step, and "
+                        "a step's resolved and host-slot tokens as two launches")
     p.add_argument("--copy-engine", choices=["auto", "vector", "bulk"], default="auto",
                    help="cow/churn: copy_blocks engine (pkv_set_copy_engine)")
     p.add_argument("--q-len", type=int, default=1,
@@ -876,7 +877,8 @@ def wl_trace(run, kind: str) -> dict:
     gen = torch.Generator(device=dev).manual_seed(2000 + run.rank)
     k = torch.randn((L, rows, es), generator=gen, device=dev, dtype=torch.bfloat16)
     v = torch.randn((L, rows, es), generator=gen, device=dev, dtype=torch.bfloat16)
-    stepper = DeviceStepper(backend, stream=stream, timing=False, fuse_copy_zero=not args.no_fuse)
+    stepper = DeviceStepper(backend, stream=stream, timing=False, fuse_copy_zero=not args.no_fuse,
+                            fuse_mixed=not args.no_fuse)
     with torch.cuda.stream(stream):
         for p in plans[: 1 + W if kind == "cow" else W]:
             stepper.apply(p, k, v)
@@ -933,6 +935,7 @@ def wl_trace(run, kind: str) -> dict:
     }
     fused = stepper.fused_steps
     out["config"]["fused_copy_zero_steps"] = fused
+    out["config"]["one_launch_token_write_steps"] = stepper.mixed_steps
     if kind == "cow" and fused:
         # Steps that ran their copies and zeroes as one launch move both in
         # the copy phase; the others zero in their own phase.
