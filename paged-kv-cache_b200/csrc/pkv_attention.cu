@@ -53,9 +53,10 @@ constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxStages = 6;
 // Pool blocks per split, at most: a CTA has a fixed cost (queries, barrier
 // set-up, the first copies' round trip, the warp merge), so long splits pay
-// best. 128 is the most the per-warp block-id prefetch holds (32 a warp);
+// best. The per-warp block-id prefetch holds 64 a warp (256 a split);
 // measured on the config-2 batch: 16 / 32 / 64 / 128 blocks gave 0.65 /
-// 0.82 / 0.89 / 0.90 of peak.
+// 0.82 / 0.89 / 0.90 of peak (bf16). fp8 tiles are half the bytes a
+// block, so fp8 pools take splits of twice as many blocks.
 #ifndef PKV_ATTN_SPLIT_BLOCKS
 #define PKV_ATTN_SPLIT_BLOCKS 128
 #endif
@@ -433,13 +434,14 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         }
     }
 
-    // This warp's block ids, one per lane (count <= 32: splits hold at most
-    // 128 blocks), read once so that no table load sits in the block loop.
+    // This warp's block ids, up to two per lane (count <= 64: splits hold at
+    // most 256 blocks), read once so that no table load sits in the block loop.
     const int my_blk = lane < count ? __ldg(table + first + kAttnWarps * lane) : -1;
+    const int my_blk2 = lane + 32 < count ? __ldg(table + first + kAttnWarps * (lane + 32)) : -1;
     uint32_t live = 0;   // bit s: stage s holds a block in flight (block id inside the pool)
     uint32_t dirty = 0;  // bit s: stage s's V rows were zeroed by generic stores
     auto issue = [&](int i, int st) {  // st == i % kStages
-        const int blk = __shfl_sync(0xffffffffu, my_blk, i);
+        const int blk = __shfl_sync(0xffffffffu, i < 32 ? my_blk : my_blk2, i & 31);
         if (blk < 0 || blk >= a.num_blocks) {
             if (lane == 0) record_error(a.err, kInvalidBlock, seq);
             live &= ~(1u << st);
@@ -972,12 +974,13 @@ cudaError_t launch_attention_plan(const int *ctx, int num_seqs, int max_ctx, uns
                       shift, order);
 }
 
-int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split) {
+int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split, bool fp8) {
     const int max_blocks = (max_ctx + kTok - 1) / kTok;
-    // At least one block per warp per split, at most PKV_ATTN_SPLIT_BLOCKS;
-    // fewer blocks per split while the (sequence, kv head) pairs alone cannot
-    // fill two CTAs per SM.
-    int p = PKV_ATTN_SPLIT_BLOCKS;
+    // At least one block per warp per split, at most PKV_ATTN_SPLIT_BLOCKS
+    // (twice that for fp8 tiles, half the bytes a block); fewer blocks per
+    // split while the (sequence, kv head) pairs alone cannot fill two CTAs
+    // per SM.
+    int p = fp8 ? 2 * PKV_ATTN_SPLIT_BLOCKS : PKV_ATTN_SPLIT_BLOCKS;
     while (p > kAttnWarps && num_pairs * ((max_blocks + p - 1) / p) < 2LL * sms) p /= 2;
     *blocks_per_split = p;
     return std::max(1, (max_blocks + p - 1) / p);

@@ -1070,7 +1070,8 @@ Status B200Backend::paged_attention_dev(int64_t layer, const void *q, DType quer
     a.layer_row0 = (int)(layer * (int64_t)(cfg_.num_blocks * cfg_.block_size));
     a.num_blocks = (int)cfg_.num_blocks;
     a.max_ctx = (int)max_ctx;
-    a.num_splits = attention_splits((long long)num_seqs * kv, (int)max_ctx, sms_, &a.blocks_per_split);
+    a.num_splits = attention_splits((long long)num_seqs * kv, (int)max_ctx, sms_, &a.blocks_per_split,
+                                    dtype_ == DType::FP8_E4M3);
     a.scale_log2 = softmax_scale * 1.4426950408889634f;
     if (dtype_ == DType::FP8_E4M3) {
         const long long stride = std::max<long long>((long long)(cfg_.num_layers * cfg_.num_kv_heads), 1);

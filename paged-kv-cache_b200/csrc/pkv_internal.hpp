@@ -244,7 +244,7 @@ cudaError_t launch_digest_rows(const DigestRowsLaunch &a, int sms, cudaStream_t 
 cudaError_t make_attention_tmaps(void *k_plane, void *v_plane, DType dtype, long long entry_elems,
                                  long long rows, int head_dim,
                                  void *tmaps_out /* 2 x 128 bytes, 64-aligned */);
-int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split);
+int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split, bool fp8);
 // The sequences ordered by descending block count (ctx entries outside
 // [0, max_ctx] count as empty, as the attention kernel treats them):
 // order[num_seqs].
