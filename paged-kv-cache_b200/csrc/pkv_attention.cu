@@ -60,6 +60,13 @@ constexpr int kMaxStages = 6;
 #ifndef PKV_ATTN_SPLIT_BLOCKS
 #define PKV_ATTN_SPLIT_BLOCKS 128
 #endif
+#ifndef PKV_ATTN_SPLIT_BLOCKS_FP8
+#define PKV_ATTN_SPLIT_BLOCKS_FP8 256
+#endif
+// Block ids a lane prefetches: splits of up to 128 * kIdsPerLane blocks.
+constexpr int kIdsPerLane =
+    ((PKV_ATTN_SPLIT_BLOCKS > PKV_ATTN_SPLIT_BLOCKS_FP8 ? PKV_ATTN_SPLIT_BLOCKS
+                                                        : PKV_ATTN_SPLIT_BLOCKS_FP8) + 127) / 128;
 constexpr int kTok = 16;                 // tokens per pool block
 constexpr int kDeviceCode = 9;           // PKV_ERR_DEVICE
 constexpr long long kAttnWaitCycles = 4000000000ll;  // about 2 s at 2 GHz
@@ -434,14 +441,20 @@ paged_attention_kernel(const __grid_constant__ CUtensorMap tk, const __grid_cons
         }
     }
 
-    // This warp's block ids, up to two per lane (count <= 64: splits hold at
-    // most 256 blocks), read once so that no table load sits in the block loop.
-    const int my_blk = lane < count ? __ldg(table + first + kAttnWarps * lane) : -1;
-    const int my_blk2 = lane + 32 < count ? __ldg(table + first + kAttnWarps * (lane + 32)) : -1;
+    // This warp's block ids, up to kIdsPerLane per lane (count <= 32 x
+    // kIdsPerLane), read once so that no table load sits in the block loop.
+    int my_blk[kIdsPerLane];
+#pragma unroll
+    for (int r = 0; r < kIdsPerLane; ++r)
+        my_blk[r] = lane + 32 * r < count ? __ldg(table + first + kAttnWarps * (lane + 32 * r)) : -1;
     uint32_t live = 0;   // bit s: stage s holds a block in flight (block id inside the pool)
     uint32_t dirty = 0;  // bit s: stage s's V rows were zeroed by generic stores
     auto issue = [&](int i, int st) {  // st == i % kStages
-        const int blk = __shfl_sync(0xffffffffu, i < 32 ? my_blk : my_blk2, i & 31);
+        int mine = my_blk[0];
+#pragma unroll
+        for (int r = 1; r < kIdsPerLane; ++r)
+            if ((i >> 5) == r) mine = my_blk[r];
+        const int blk = __shfl_sync(0xffffffffu, mine, i & 31);
         if (blk < 0 || blk >= a.num_blocks) {
             if (lane == 0) record_error(a.err, kInvalidBlock, seq);
             live &= ~(1u << st);
@@ -980,7 +993,7 @@ int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_
     // (twice that for fp8 tiles, half the bytes a block); fewer blocks per
     // split while the (sequence, kv head) pairs alone cannot fill two CTAs
     // per SM.
-    int p = fp8 ? 2 * PKV_ATTN_SPLIT_BLOCKS : PKV_ATTN_SPLIT_BLOCKS;
+    int p = fp8 ? PKV_ATTN_SPLIT_BLOCKS_FP8 : PKV_ATTN_SPLIT_BLOCKS;
     while (p > kAttnWarps && num_pairs * ((max_blocks + p - 1) / p) < 2LL * sms) p /= 2;
     *blocks_per_split = p;
     return std::max(1, (max_blocks + p - 1) / p);
