@@ -53,12 +53,13 @@ constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxStages = 6;
 // Pool blocks per split, at most: a CTA has a fixed cost (queries, barrier
 // set-up, the first copies' round trip, the warp merge), so long splits pay
-// best. The per-warp block-id prefetch holds 64 a warp (256 a split);
-// measured on the config-2 batch: 16 / 32 / 64 / 128 blocks gave 0.65 /
-// 0.82 / 0.89 / 0.90 of peak (bf16). fp8 tiles are half the bytes a
-// block, so fp8 pools take splits of twice as many blocks.
+// best. Measured on the config-2 batch (bf16, one launch per layer, early
+// form): 16 / 32 / 64 / 128 blocks gave 0.65 / 0.82 / 0.89 / 0.90 of peak;
+// later, with the plan and 28 layers per step, 256 against 128 blocks gave
+// 1.052 against 0.994 (bf16) and 0.962 against 0.811 (fp8, whose blocks are
+// half the bytes); 512 for fp8 gave 0.949.
 #ifndef PKV_ATTN_SPLIT_BLOCKS
-#define PKV_ATTN_SPLIT_BLOCKS 128
+#define PKV_ATTN_SPLIT_BLOCKS 256
 #endif
 #ifndef PKV_ATTN_SPLIT_BLOCKS_FP8
 #define PKV_ATTN_SPLIT_BLOCKS_FP8 256
@@ -990,9 +991,8 @@ cudaError_t launch_attention_plan(const int *ctx, int num_seqs, int max_ctx, uns
 int attention_splits(long long num_pairs, int max_ctx, int sms, int *blocks_per_split, bool fp8) {
     const int max_blocks = (max_ctx + kTok - 1) / kTok;
     // At least one block per warp per split, at most PKV_ATTN_SPLIT_BLOCKS
-    // (twice that for fp8 tiles, half the bytes a block); fewer blocks per
-    // split while the (sequence, kv head) pairs alone cannot fill two CTAs
-    // per SM.
+    // (PKV_ATTN_SPLIT_BLOCKS_FP8 for fp8 tiles); fewer blocks per split while
+    // the (sequence, kv head) pairs alone cannot fill two CTAs per SM.
     int p = fp8 ? PKV_ATTN_SPLIT_BLOCKS_FP8 : PKV_ATTN_SPLIT_BLOCKS;
     while (p > kAttnWarps && num_pairs * ((max_blocks + p - 1) / p) < 2LL * sms) p /= 2;
     *blocks_per_split = p;
