@@ -152,14 +152,7 @@ inline int layers_per_chunk(long long items, long long num_layers, int sms, long
     const long long wave = (long long)sms * 4 * kThreads;
     const long long needed = (wave + std::max<long long>(items, 1) - 1) / std::max<long long>(items, 1);
     const long long cap = std::max<long long>(1, (num_layers + 3) / 4);
-    long long c = std::min<long long>(std::max<long long>(needed, 1), cap);
-    // Rounding `needed` up can overshoot one wave of 4 CTAs per SM, which
-    // sends the launch to the 2-CTAs-per-SM form and into a second and third
-    // wave; keep the chunks that still fit one wave (a decode-size scatter
-    // of many layers: 226 tokens x 80 layers of 2 KiB entries).
-    const long long ctas = std::max<long long>(1, (items + kThreads - 1) / kThreads);
-    const long long fit = (long long)sms * 4 / ctas;
-    if (c > 1 && c * ctas > (long long)sms * 4 && fit >= 1) c = std::min(c, fit);
+    const long long c = std::min<long long>(std::max<long long>(needed, 1), cap);
     const int lpc = (int)((num_layers + c - 1) / c);
     *chunks = (num_layers + lpc - 1) / lpc;
     return lpc;
