@@ -407,7 +407,9 @@ int pkv_resolve_and_cache_noalloc(const pkv_config *cfg, int pool_dtype, int sha
  * pinned chunks while earlier chunks cross the host link, and the call
  * returns once every row has been read. Environment, read by pkv_create:
  * PKV_HOST_THREADS=n sets the count (default: one per host core, at most
- * 16); PKV_HOST_STAGING=off copies from the caller's buffer instead. No
+ * 16, and at most half the ring's chunks); PKV_HOST_STAGING=off copies from
+ * the caller's buffer instead; PKV_STAGE_CHUNK_KIB and PKV_STAGE_SLOTS size
+ * the ring (default 1,024 KiB x 32, at most 64 chunks). No
  * counterpart in the reference (its CudaBackend copies each slice with a
  * fresh device allocation, crates/paged-kv-cuda/src/backend.rs:177-180). */
 int pkv_host_threads(const pkv_backend *b, int *threads);
