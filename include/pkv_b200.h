@@ -403,7 +403,7 @@ int pkv_resolve_and_cache_noalloc(const pkv_config *cfg, int pool_dtype, int sha
 /* Worker threads of the backend's host stager. Large host-buffer writes
  * (pkv_write_kv_batch / pkv_write_kv of at least 1 MiB of rows) use it when
  * the rows are in pageable memory, or are f32 rows for a bf16 pool: the
- * workers copy (or narrow to bf16) the caller's rows into a 64 MiB ring of
+ * workers copy (or narrow to bf16) the caller's rows into a 32 MiB ring of
  * pinned chunks while earlier chunks cross the host link, and the call
  * returns once every row has been read. Environment, read by pkv_create:
  * PKV_HOST_THREADS=n sets the count (default: one per host core, at most
