@@ -42,3 +42,27 @@ def test_reference_arm_line():
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert "workload" in d["config"]
+    # The same config as the device arm's line, plus the thread count; the
+    # single-threaded figure of CpuBackend (which is single-threaded) beside it.
+    assert d["config"]["host_threads"] == cb["cores"]
+    assert d["config"]["tokens_per_step"] == 65536 and d["config"]["layers"] == 28
+    assert d["config"]["workload"].startswith("ragged prefill chunk x1")
+    st = d["single_thread"]
+    assert st["cores"] == 1 and st["value"] > 0 and st["unit"] == "tokens/s"
+
+
+def test_reference_arm_maps_no_device_library():
+    """The reference arm runs only CpuBackend semantics (the oracle): it must
+    not map the device library, which `import pagedkv` no longer loads."""
+    code = (
+        "import sys; sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '1']\n"
+        "import bench; bench.main()\n"
+        "maps = [l.split()[-1] for l in open('/proc/self/maps') if '.so' in l]\n"
+        "print('LIBS', sorted(set(m for m in maps if 'pagedkv_b200' in m or 'liboracle' in m)))\n")
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join(
+        [str(ROOT), str(ROOT / "paged-kv-cache_b200"), os.environ.get("PYTHONPATH", "")]))
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True,
+                         text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    libs = [l for l in out.stdout.splitlines() if l.startswith("LIBS")][0]
+    assert "liboracle.so" in libs and "pagedkv_b200" not in libs
