@@ -161,3 +161,44 @@ def test_bad_destination_mid_batch_applies_the_prefix_like_cpubackend(cuda):
     b.write_kv_batch_pairs(0, np.ascontiguousarray(pairs[:3210]), k[:3210] * 0, v[:3210] * 0)
     assert b.device_error() is None
     assert int(np.count_nonzero(b.planes()[0].float().cpu().numpy())) == 0
+
+
+@pytest.mark.parametrize("pool,host", [("f16", "f32"), ("fp8_e4m3", "bf16"), ("f32", "f32")])
+def test_staged_copies_for_other_pool_types_equal_the_unstaged_path(cuda, monkeypatch, pool, host):
+    """Pageable rows the stager copies unchanged (no host narrowing) and the
+    device then converts or quantises: the same pool as the direct path."""
+    import torch
+
+    nbytes = {"f16": 2, "fp8_e4m3": 1, "f32": 4}[pool]
+    cfg = CacheConfig(num_blocks=512, block_size=16, num_kv_heads=2, head_dim=128, num_layers=2,
+                      dtype_bytes=nbytes)
+    e = cfg.entry_elems()
+    t = 4000
+    st = Stream(91)
+    slots = st.permutation(cfg.num_blocks * cfg.block_size)[:t].astype(np.int64)
+    k = (st.normal(t * e) * 2).astype(np.float32).reshape(t, e)
+    v = (st.normal(t * e) * 2).astype(np.float32).reshape(t, e)
+    if host == "bf16":
+        k, v = f32_to_bf16_bits(k), f32_to_bf16_bits(v)
+    pools = []
+    for mode in ("auto", "off"):
+        monkeypatch.setenv("PKV_HOST_STAGING", mode)
+        b = B200Backend(cfg, dtype=pool)
+        if pool == "fp8_e4m3":
+            b.set_kv_scales(np.full((2, 2), 0.5, np.float32), np.full((2, 2), 0.25, np.float32))
+        b.write_kv_batch_slots(1, slots // 16, slots % 16, k, v, host_dtype=host)
+        assert b.device_error() is None
+        pools.append([p.view(torch.uint8).cpu().numpy() for p in b.planes()])
+        b.close()
+    for a, c in zip(pools[0], pools[1]):
+        np.testing.assert_array_equal(a, c)
+    assert np.count_nonzero(pools[0][0]) > 0
+
+
+def test_stager_settings_from_the_environment(cuda, monkeypatch):
+    cfg = CacheConfig(num_blocks=16, block_size=16, num_kv_heads=1, head_dim=64, num_layers=1,
+                      dtype_bytes=2)
+    monkeypatch.setenv("PKV_HOST_THREADS", "3")
+    assert B200Backend(cfg, dtype="bf16").host_threads() == 3
+    monkeypatch.setenv("PKV_STAGE_SLOTS", "4")  # at most half the ring's chunks
+    assert B200Backend(cfg, dtype="bf16").host_threads() == 2
