@@ -6,7 +6,8 @@ and block tables on every rank, so nothing crosses GPUs on the data path.
 Verification exchanges only 64-bit digests: every rank digests its shard and
 the rows it was given (element hashes over global indices), the ranks
 all-gather the four numbers, and the shard digests must add up (mod 2^64) to
-the digest of what was written.
+the digest of what was written. For small pools, gather_shards reassembles
+the whole pool on rank 0 from the shards.
 """
 
 from __future__ import annotations
@@ -52,3 +53,29 @@ def verify_over_group(pool: tuple[int, int], expected: tuple[int, int], device=N
         "pool_digest_v": f"{tot[1]:016x}",
         "collective": how,
     }
+
+
+def gather_shards(k_plane, v_plane, device=None):
+    """The full pool reassembled on rank 0 from every rank's head shard.
+
+    k_plane, v_plane: this rank's shard planes [L][NB][bs][E/G] (torch
+    tensors; on the GPU for NCCL, on the CPU for gloo). Every rank sends its
+    shard; rank 0 concatenates the slices along the entry axis in rank order
+    and returns (K, V) [L][NB][bs][E]; other ranks return None. For pools
+    that fit one rank's memory G times over: a check for tests and small
+    configurations, beside the digest verification above."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return k_plane, v_plane
+    world = dist.get_world_size()
+    out = []
+    for p in (k_plane, v_plane):
+        src = p.contiguous()
+        if device is not None:
+            src = src.to(device)
+        parts = [torch.empty_like(src) for _ in range(world)]
+        dist.all_gather(parts, src)  # gather is not available on every backend
+        out.append(torch.cat(parts, dim=-1) if dist.get_rank() == 0 else None)
+    return tuple(out) if dist.get_rank() == 0 else None

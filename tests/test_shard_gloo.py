@@ -165,3 +165,52 @@ def test_rank_breakdown_over_two_gloo_ranks(tmp_path):
     assert o["steps_bounded_by_rank"] == [3, 2]
     fr = o["token_write_frac_of_peak_per_rank"]
     assert abs(fr[0] / fr[1] - 2.0) < 1e-9  # rank 1 took twice as long for the same bytes
+
+
+def _gather_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    """Each rank holds its head shard of a pool written through the oracle;
+    rank 0 reassembles the full pool from the shards and compares it, element
+    for element, with the pool the oracle writes unsharded."""
+    sys.path[:0] = [str(ROOT / "paged-kv-cache_b200"), str(ROOT)]
+    import torch
+    import torch.distributed as dist
+
+    from oracle.cpu import OracleBackend
+    from pagedkv.config import CacheConfig
+    from pagedkv.shard import entry_slice, gather_shards
+    from pagedkv.workloads import Stream
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = CacheConfig(num_blocks=12, block_size=4, num_kv_heads=4, head_dim=8, num_layers=2,
+                      dtype_bytes=4)
+    e = cfg.entry_elems()
+    off, w = entry_slice(e, rank, world)
+    st = Stream(3)
+    t = 30
+    slots = st.permutation(cfg.num_blocks * cfg.block_size)[:t]
+    dsts = [(int(s) // 4, int(s) % 4) for s in slots]
+    full = OracleBackend(cfg)
+    for layer in range(cfg.num_layers):
+        k = st.normal(t * e).astype(np.float32).reshape(t, e)
+        v = st.normal(t * e).astype(np.float32).reshape(t, e)
+        full.write_kv_batch(layer, dsts, k.ravel(), v.ravel())
+    fk, fv = full.planes()
+    # This rank's shard: its slice of the entry axis.
+    mine = (torch.from_numpy(np.ascontiguousarray(fk[..., off:off + w])),
+            torch.from_numpy(np.ascontiguousarray(fv[..., off:off + w])))
+    got = gather_shards(*mine)
+    if rank == 0:
+        ok = np.array_equal(got[0].numpy(), fk) and np.array_equal(got[1].numpy(), fv)
+        Path(out_dir, "gather.txt").write_text(str(ok))
+    else:
+        assert got is None
+    dist.destroy_process_group()
+
+
+def test_shards_gathered_to_rank_zero_reassemble_the_pool(tmp_path):
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_gather_rank_main, args=(2, 29535, str(tmp_path)), nprocs=2,
+                       start_method="spawn", join=True)
+    assert Path(tmp_path, "gather.txt").read_text() == "True"
